@@ -1,0 +1,161 @@
+/*
+ * droidcorr.h -- C ABI of the B200 (sm_100a) DROID-SLAM correlation library
+ * (libdroidcorr.so).
+ *
+ * It replaces the correlation hot path of slam-hands (cuda_slam/main.cu and its
+ * copy in cuda_pipeline/slam.cuh):
+ *
+ *   reference                                             replaced by
+ *   ----------------------------------------------------  ---------------------------
+ *   DroidState::fmaps / add_keyframe  main.cu:677, :755    dc_set_frames
+ *   CudaDroid::build_correlation      main.cu:1500-1526    dc_build_volume (M = 1)
+ *   (cublasGemmEx + cuDNN avg_pool2d, nn.cuh:389-410)
+ *   avg_pool_2x2_kernel               main.cu:1150-1170    dc_pool_2x2
+ *   CudaDroid::sample_correlation     main.cu:1529-1552    dc_lookup (M = 1)
+ *   (corr_index_kernel                main.cu:1079-1114)
+ *   batch_corr_sample_kernel x4       main.cu:1175-1217    dc_lookup
+ *   CudaDroid::batch_build_and_sample_correlation          dc_build_and_lookup
+ *                                     main.cu:1555-1613
+ *   (no reference counterpart: on-the-fly lookup)          dc_alt_lookup
+ *   cuda_pipeline/slam.cuh:2796, :2825, :2851              the same three entry points
+ *
+ * Conventions (all entry points):
+ *   - Every pointer argument named *_dev is DEVICE memory owned by the caller
+ *     (the reference's GpuBuf buffers, nn.cuh:45-71).  The library owns only its
+ *     context: the packed feature-map store and its scratch.
+ *   - Work is enqueued on the given stream; no call synchronises the host except
+ *     dc_create / dc_destroy.  A context may be used by one host thread at a time.
+ *   - Return value: DC_OK (0) or a DC_ERR_* status.  Nothing exits the process
+ *     (the reference's CUDA_CHECK -> exit(1), nn.cuh:17-41, is replaced by status
+ *     codes).  dc_last_error() returns a message for the last failure.
+ *
+ * Layouts (identical to the reference):
+ *   fmaps     [count][C][h][w]            fp32 or fp16, one slot per keyframe
+ *   ii, jj    [M] int32 (device)           edge e correlates source frame ii[e]
+ *                                          (pixels p) with target frame jj[e] (q)
+ *   vol_l     [M][h*w][h>>l][w>>l] fp32    level-l volume, V_l[e][p][y][x]
+ *   coords    [M][2][h][w] fp32            ch0 = x, ch1 = y, target pixels at 1/8 res
+ *   out       [M][levels*(2r+1)^2][h][w]   channel l*(2r+1)^2 + a*(2r+1) + b,
+ *                                          a = x offset, b = y offset (main.cu:1203-1213)
+ */
+#ifndef DROIDCORR_H_
+#define DROIDCORR_H_
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same type as cudaStream_t / CUstream. */
+typedef struct CUstream_st* dc_stream_t;
+typedef struct dc_ctx dc_ctx;
+
+/* status codes */
+#define DC_OK 0
+#define DC_ERR_INVALID_ARG 1
+#define DC_ERR_CUDA 2
+#define DC_ERR_UNSUPPORTED 3
+#define DC_ERR_NO_MEMORY 4
+#define DC_ERR_DEVICE_TIMEOUT 5
+#define DC_ERR_NOT_READY 6
+
+/* Arithmetic of the correlation dot products (the volume build).
+ *   DC_PREC_FP32  exact fp32 FFMA, channels accumulated in order c = 0..C-1
+ *   DC_PREC_TF32  inputs rounded to TF32, fp32 accumulate (tensor cores)
+ *   DC_PREC_BF16  inputs rounded to BF16, fp32 accumulate (tensor cores)
+ *   DC_PREC_FP16  inputs rounded to FP16, fp32 accumulate (tensor cores) --
+ *                 the reference's own arithmetic (FP16 fmaps, cublasGemmBatchedEx
+ *                 with CUBLAS_COMPUTE_32F, main.cu:1573-1581). */
+#define DC_PREC_FP32 0
+#define DC_PREC_TF32 1
+#define DC_PREC_BF16 2
+#define DC_PREC_FP16 3
+
+/* element type of caller feature maps */
+#define DC_DTYPE_F32 0
+#define DC_DTYPE_F16 1
+
+typedef struct dc_config {
+    int h, w;        /* feature grid (image / 8), e.g. 48 x 64 */
+    int channels;    /* C: 32, 64, 128 or 256 (128 in DROID-SLAM) */
+    int levels;      /* pyramid levels, 1..4 (reference: 4, main.cu:1604) */
+    int radius;      /* lookup radius, 0..3 (reference: 3, main.cu:1531) */
+    int max_frames;  /* keyframe slots in the store (DroidState::MAX_KEYFRAMES) */
+    int max_edges;   /* largest M of one call (reference chunk: MAX_BATCH_EDGES = 48) */
+    int precision;   /* DC_PREC_* */
+    float alpha;     /* volume scale; the reference uses 1/16 (main.cu:1506, :1572) */
+} dc_config;
+
+/* Fill *cfg with the reference defaults for an h x w grid:
+ * C = 128, levels = 4, radius = 3, max_frames = 512, max_edges = 48,
+ * precision = DC_PREC_FP16, alpha = 1/16. */
+void dc_default_config(dc_config* cfg, int h, int w);
+
+/* Create a context on the current CUDA device.  Allocates the feature-map store
+ * (max_frames slots).  Replaces the correlation part of CudaDroid::init,
+ * main.cu:1405-1426. */
+int dc_create(const dc_config* cfg, dc_ctx** out);
+int dc_destroy(dc_ctx* ctx);
+const char* dc_last_error(const dc_ctx* ctx);
+const char* dc_status_string(int status);
+
+/* Bytes of device memory the context holds. */
+long long dc_context_bytes(const dc_ctx* ctx);
+
+/* Pack `count` feature maps into store slots first_slot .. first_slot+count-1
+ * (the library's resident copy of DroidState::fmaps, main.cu:677, written by
+ * add_keyframe, main.cu:755).  fmaps_dev: [count][C][h][w], dtype DC_DTYPE_*.
+ * The store keeps, per slot, the map and its 2x2-average pyramid in the
+ * precision's element type, pixel-major.  Must be called again for a slot
+ * whenever its feature map changes. */
+int dc_set_frames(dc_ctx* ctx, const void* fmaps_dev, int dtype, int first_slot, int count,
+                  dc_stream_t stream);
+
+/* Materialised volumes for M edges (CudaDroid::build_correlation, main.cu:1500,
+ * and steps 1-3 of batch_build_and_sample_correlation, main.cu:1558-1596):
+ * vol0 = alpha * f_ii^T f_jj, then vol_l = 2x2 average of vol_{l-1} over the
+ * target axes (cascaded, floor on odd dims).  vols_dev: host array of `levels`
+ * device pointers; entries 1.. may be NULL to skip those levels. */
+int dc_build_volume(dc_ctx* ctx, const int* ii_dev, const int* jj_dev, int M,
+                    float* const* vols_dev, dc_stream_t stream);
+
+/* One 2x2 average-pool level, in [N][H][W] -> out [N][H/2][W/2]
+ * (avg_pool_2x2_kernel, main.cu:1150-1170).  Bit-identical to the reference. */
+int dc_pool_2x2(const float* in_dev, float* out_dev, long long N, int H, int W,
+                dc_stream_t stream);
+
+/* Radius-r bilinear lookup from materialised volumes (batch_corr_sample_kernel,
+ * main.cu:1175-1217, all levels in one launch; out is written, not accumulated,
+ * so no memset is needed).  vols_dev: host array of `levels` device pointers.
+ * Bit-identical to the reference kernel for the same volumes. */
+int dc_lookup(dc_ctx* ctx, const float* const* vols_dev, const float* coords_dev,
+              float* out_dev, int M, dc_stream_t stream);
+
+/* The corr_index_kernel arithmetic (single-edge sample_correlation,
+ * main.cu:1529-1552: each tap's weighted value rounded, then added). */
+int dc_lookup_single(dc_ctx* ctx, const float* const* vols_dev, const float* coords_dev,
+                     float* out_dev, dc_stream_t stream);
+
+/* Build + pyramid + lookup for M edges without storing any volume
+ * (batch_build_and_sample_correlation, main.cu:1555-1613).  Reads source and
+ * target maps from store slots ii[e], jj[e].  Pooled levels are computed as
+ * alpha * <f_ii, P_l f_jj> (P_l = l-fold 2x2 average of the target map), equal to
+ * pooling the volume because pooling is linear. */
+int dc_build_and_lookup(dc_ctx* ctx, const int* ii_dev, const int* jj_dev, int M,
+                        const float* coords_dev, float* out_dev, dc_stream_t stream);
+
+/* On-the-fly ("alt-corr") lookup: same result as dc_build_and_lookup, computed as
+ * per-pixel gathered dot products against the pooled target maps (only the
+ * (2r+2)^2 taps of each level), never forming a volume row.  Memory per edge is
+ * the output only.  No reference counterpart (the reference always
+ * materialises, main.cu:2185-2201). */
+int dc_alt_lookup(dc_ctx* ctx, const int* ii_dev, const int* jj_dev, int M,
+                  const float* coords_dev, float* out_dev, dc_stream_t stream);
+
+/* Number of kernel launches the library has issued on this context (for
+ * launch accounting in benchmarks). */
+long long dc_launch_count(const dc_ctx* ctx);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DROIDCORR_H_ */

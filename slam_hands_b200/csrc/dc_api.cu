@@ -1,0 +1,200 @@
+// dc_api.cu -- the C ABI of libdroidcorr: argument validation, the context and
+// dispatch to the kernels.  Declarations and the reference interface each entry
+// point replaces are in include/droidcorr.h.
+#include <cstdio>
+#include <cstring>
+
+#include "dc_internal.cuh"
+
+int dc_fail(dc_ctx* ctx, int status, const std::string& msg) {
+    if (ctx) ctx->err = msg;
+    return status;
+}
+
+int dc_check_launch(dc_ctx* ctx, const char* what) {
+    ctx->launches++;
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess)
+        return dc_fail(ctx, DC_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+    return DC_OK;
+}
+
+namespace {
+
+int validate_edges(dc_ctx* ctx, const int* ii, const int* jj, int M) {
+    if (M < 0 || M > ctx->cfg.max_edges)
+        return dc_fail(ctx, DC_ERR_INVALID_ARG,
+                       "M=" + std::to_string(M) + " outside [0, max_edges=" +
+                           std::to_string(ctx->cfg.max_edges) + "]");
+    if (M > 0 && (!ii || !jj)) return dc_fail(ctx, DC_ERR_INVALID_ARG, "ii/jj is NULL");
+    return DC_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+void dc_default_config(dc_config* cfg, int h, int w) {
+    cfg->h = h;
+    cfg->w = w;
+    cfg->channels = 128;
+    cfg->levels = 4;
+    cfg->radius = 3;
+    cfg->max_frames = 512;
+    cfg->max_edges = 48;
+    cfg->precision = DC_PREC_FP16;
+    cfg->alpha = 1.0f / 16.0f;
+}
+
+const char* dc_status_string(int s) {
+    switch (s) {
+        case DC_OK: return "ok";
+        case DC_ERR_INVALID_ARG: return "invalid argument";
+        case DC_ERR_CUDA: return "CUDA error";
+        case DC_ERR_UNSUPPORTED: return "unsupported configuration";
+        case DC_ERR_NO_MEMORY: return "out of device memory";
+        case DC_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
+        case DC_ERR_NOT_READY: return "not ready";
+        default: return "unknown status";
+    }
+}
+
+int dc_create(const dc_config* cfg, dc_ctx** out) {
+    if (!cfg || !out) return DC_ERR_INVALID_ARG;
+    *out = nullptr;
+    const dc_config& c = *cfg;
+    if (c.h < 1 || c.w < 1 || (long long)c.h * c.w > DC_MAX_HW) return DC_ERR_INVALID_ARG;
+    if (c.channels != 32 && c.channels != 64 && c.channels != 128 && c.channels != 256)
+        return DC_ERR_INVALID_ARG;
+    if (c.levels < 1 || c.levels > DC_MAX_LEVELS) return DC_ERR_INVALID_ARG;
+    if (c.radius < 0 || c.radius > DC_MAX_RADIUS) return DC_ERR_INVALID_ARG;
+    if (c.max_frames < 1 || c.max_edges < 1) return DC_ERR_INVALID_ARG;
+    if (c.precision < DC_PREC_FP32 || c.precision > DC_PREC_FP16) return DC_ERR_INVALID_ARG;
+    if ((c.h >> (c.levels - 1)) < 1 || (c.w >> (c.levels - 1)) < 1) return DC_ERR_INVALID_ARG;
+
+    dc_ctx* ctx = new dc_ctx();
+    ctx->cfg = c;
+    if (cudaGetDevice(&ctx->device) != cudaSuccess) {
+        delete ctx;
+        return DC_ERR_CUDA;
+    }
+    cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, ctx->device);
+    ctx->hw = c.h * c.w;
+    long long rows = 0;
+    for (int l = 0; l < DC_MAX_LEVELS; l++) {
+        ctx->H[l] = c.h >> l;
+        ctx->W[l] = c.w >> l;
+        ctx->level_row0[l] = rows;
+        if (l < c.levels) {
+            long long n = (long long)ctx->H[l] * ctx->W[l];
+            rows += (n + DC_ROW_PAD - 1) / DC_ROW_PAD * DC_ROW_PAD;
+        }
+    }
+    ctx->frame_rows = rows;
+    ctx->elem_bytes = (c.precision == DC_PREC_FP16 || c.precision == DC_PREC_BF16) ? 2 : 4;
+    ctx->store_bytes = (long long)c.max_frames * rows * c.channels * ctx->elem_bytes;
+    if (cudaMalloc(&ctx->store, ctx->store_bytes) != cudaSuccess) {
+        cudaGetLastError();
+        delete ctx;
+        return DC_ERR_NO_MEMORY;
+    }
+    // Padding rows must read as zero; the store is written slot by slot later.
+    if (cudaMemset(ctx->store, 0, ctx->store_bytes) != cudaSuccess ||
+        cudaDeviceSynchronize() != cudaSuccess) {
+        cudaFree(ctx->store);
+        delete ctx;
+        return DC_ERR_CUDA;
+    }
+    *out = ctx;
+    return DC_OK;
+}
+
+int dc_destroy(dc_ctx* ctx) {
+    if (!ctx) return DC_OK;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(ctx->device);
+    if (ctx->store) cudaFree(ctx->store);
+    if (prev >= 0) cudaSetDevice(prev);
+    delete ctx;
+    return DC_OK;
+}
+
+const char* dc_last_error(const dc_ctx* ctx) { return ctx ? ctx->err.c_str() : "null context"; }
+
+long long dc_context_bytes(const dc_ctx* ctx) { return ctx ? ctx->store_bytes : 0; }
+
+long long dc_launch_count(const dc_ctx* ctx) { return ctx ? ctx->launches : 0; }
+
+int dc_set_frames(dc_ctx* ctx, const void* fmaps, int dtype, int first, int count,
+                  dc_stream_t stream) {
+    if (!ctx) return DC_ERR_INVALID_ARG;
+    if (dtype != DC_DTYPE_F32 && dtype != DC_DTYPE_F16)
+        return dc_fail(ctx, DC_ERR_INVALID_ARG, "dtype must be DC_DTYPE_F32 or DC_DTYPE_F16");
+    if (first < 0 || count < 0 || first + count > ctx->cfg.max_frames)
+        return dc_fail(ctx, DC_ERR_INVALID_ARG, "slot range outside [0, max_frames)");
+    if (count == 0) return DC_OK;
+    if (!fmaps) return dc_fail(ctx, DC_ERR_INVALID_ARG, "fmaps is NULL");
+    return dc_launch_store(ctx, fmaps, dtype, first, count, (cudaStream_t)stream);
+}
+
+int dc_build_volume(dc_ctx* ctx, const int* ii, const int* jj, int M, float* const* vols,
+                    dc_stream_t stream) {
+    if (!ctx) return DC_ERR_INVALID_ARG;
+    int rc = validate_edges(ctx, ii, jj, M);
+    if (rc) return rc;
+    if (!vols || !vols[0]) return dc_fail(ctx, DC_ERR_INVALID_ARG, "vols[0] is NULL");
+    if (M == 0) return DC_OK;
+    rc = dc_launch_volume_ffma(ctx, ii, jj, M, vols[0], (cudaStream_t)stream);
+    if (rc) return rc;
+    return dc_launch_volume_pyramid(ctx, vols, M, (cudaStream_t)stream);
+}
+
+int dc_pool_2x2(const float* in, float* out, long long N, int H, int W, dc_stream_t stream) {
+    if (N < 0 || H < 0 || W < 0) return DC_ERR_INVALID_ARG;
+    if (N == 0 || H < 2 || W < 2) return DC_OK;
+    if (!in || !out) return DC_ERR_INVALID_ARG;
+    return dc_launch_pool2x2(in, out, N, H, W, (cudaStream_t)stream);
+}
+
+int dc_lookup(dc_ctx* ctx, const float* const* vols, const float* coords, float* out, int M,
+              dc_stream_t stream) {
+    if (!ctx) return DC_ERR_INVALID_ARG;
+    if (M < 0) return dc_fail(ctx, DC_ERR_INVALID_ARG, "M < 0");
+    if (M == 0) return DC_OK;
+    if (!vols || !coords || !out) return dc_fail(ctx, DC_ERR_INVALID_ARG, "NULL pointer");
+    for (int l = 0; l < ctx->cfg.levels; l++)
+        if (!vols[l]) return dc_fail(ctx, DC_ERR_INVALID_ARG, "vols[l] is NULL");
+    return dc_launch_lookup(ctx, vols, coords, out, M, false, (cudaStream_t)stream);
+}
+
+int dc_lookup_single(dc_ctx* ctx, const float* const* vols, const float* coords, float* out,
+                     dc_stream_t stream) {
+    if (!ctx) return DC_ERR_INVALID_ARG;
+    if (!vols || !coords || !out) return dc_fail(ctx, DC_ERR_INVALID_ARG, "NULL pointer");
+    for (int l = 0; l < ctx->cfg.levels; l++)
+        if (!vols[l]) return dc_fail(ctx, DC_ERR_INVALID_ARG, "vols[l] is NULL");
+    return dc_launch_lookup(ctx, vols, coords, out, 1, true, (cudaStream_t)stream);
+}
+
+int dc_build_and_lookup(dc_ctx* ctx, const int* ii, const int* jj, int M, const float* coords,
+                        float* out, dc_stream_t stream) {
+    if (!ctx) return DC_ERR_INVALID_ARG;
+    int rc = validate_edges(ctx, ii, jj, M);
+    if (rc) return rc;
+    if (M == 0) return DC_OK;
+    if (!coords || !out) return dc_fail(ctx, DC_ERR_INVALID_ARG, "NULL pointer");
+    return dc_launch_alt(ctx, ii, jj, M, coords, out, (cudaStream_t)stream);
+}
+
+int dc_alt_lookup(dc_ctx* ctx, const int* ii, const int* jj, int M, const float* coords,
+                  float* out, dc_stream_t stream) {
+    if (!ctx) return DC_ERR_INVALID_ARG;
+    int rc = validate_edges(ctx, ii, jj, M);
+    if (rc) return rc;
+    if (M == 0) return DC_OK;
+    if (!coords || !out) return dc_fail(ctx, DC_ERR_INVALID_ARG, "NULL pointer");
+    return dc_launch_alt(ctx, ii, jj, M, coords, out, (cudaStream_t)stream);
+}
+
+}  // extern "C"

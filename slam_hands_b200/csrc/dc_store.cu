@@ -1,0 +1,108 @@
+// dc_store.cu -- packing keyframe feature maps into the resident store.
+//
+// Input: the reference's per-keyframe layout [C][h][w] (DroidState::fmaps,
+// cuda_slam/main.cu:677).  Output per slot: the map and its cascaded 2x2-average
+// pyramid P_1..P_{L-1} (the same average as avg_pool_2x2_kernel,
+// main.cu:1150-1170, applied to the map instead of the volume), pixel-major
+// [pixels][C] in the precision's element type, so that one target pixel's
+// channel vector is one contiguous row (coalesced gathers, K-major tensor-core
+// operand tiles).
+//
+// One CTA packs one 8x8 tile of level-0 pixels of one slot.  With floor-pooling,
+// every level-l cell lies inside exactly one such tile (cell (y, x) of level l
+// covers level-0 rows [y 2^l, (y+1) 2^l), and 2^l divides 8), so tiles partition
+// all levels and each map element is read from HBM once.
+#include "dc_internal.cuh"
+
+namespace {
+
+template <typename T>
+__device__ __forceinline__ T pack_value(float v, bool tf32) {
+    if (tf32) v = dc::round_tf32(v);
+    return dc::from_f32<T>(v);
+}
+
+template <typename Tin, typename T>
+__global__ void __launch_bounds__(256) store_pack_kernel(const Tin* __restrict__ fmaps,
+                                                          T* __restrict__ store, dc::Geom g,
+                                                          int first, bool tf32) {
+    extern __shared__ float sm[];
+    const int C = g.C;
+    float* t0 = sm;             // [C][64]  level 0, tile-local (ty*8+tx)
+    float* t1 = t0 + C * 64;    // [C][16]  level 1
+    float* t2 = t1 + C * 16;    // [C][4]   level 2
+    float* t3 = t2 + C * 4;     // [C][1]   level 3
+    const int slot_local = blockIdx.z;
+    const int slot = first + slot_local;
+    const int x0 = blockIdx.x * 8, y0 = blockIdx.y * 8;
+    const Tin* f = fmaps + (size_t)slot_local * C * g.hw;
+    T* st = store + (size_t)slot * g.frame_rows * C;
+
+    for (int idx = threadIdx.x; idx < C * 64; idx += blockDim.x) {
+        int c = idx >> 6, k = idx & 63;
+        int y = y0 + (k >> 3), x = x0 + (k & 7);
+        float v = 0.0f;
+        if (y < g.h && x < g.w) v = dc::to_f32(f[(size_t)c * g.hw + y * g.w + x]);
+        t0[idx] = v;
+    }
+    __syncthreads();
+    // level 0 rows
+    for (int idx = threadIdx.x; idx < C * 64; idx += blockDim.x) {
+        int k = idx / C, c = idx % C;
+        int y = y0 + (k >> 3), x = x0 + (k & 7);
+        if (y < g.h && x < g.w)
+            st[(g.row0[0] + y * g.w + x) * C + c] = pack_value<T>(t0[c * 64 + k], tf32);
+    }
+    // cascaded pooling inside the tile: level l has (8 >> l)^2 tile-local cells
+    float* src = t0;
+    float* dstv[3] = {t1, t2, t3};
+    for (int l = 1; l < g.levels; l++) {
+        const int sw = 8 >> (l - 1), dw = 8 >> l;  // tile-local widths
+        float* dst = dstv[l - 1];
+        for (int idx = threadIdx.x; idx < C * dw * dw; idx += blockDim.x) {
+            int c = idx / (dw * dw), k = idx % (dw * dw);
+            int ly = k / dw, lx = k % dw;
+            const float* s = src + c * sw * sw;
+            float v = s[(2 * ly) * sw + 2 * lx] + s[(2 * ly) * sw + 2 * lx + 1];
+            v = v + s[(2 * ly + 1) * sw + 2 * lx];
+            v = v + s[(2 * ly + 1) * sw + 2 * lx + 1];
+            dst[idx] = 0.25f * v;
+        }
+        __syncthreads();
+        const int gy0 = y0 >> l, gx0 = x0 >> l;
+        for (int idx = threadIdx.x; idx < C * dw * dw; idx += blockDim.x) {
+            int k = idx / C, c = idx % C;
+            int y = gy0 + k / dw, x = gx0 + k % dw;
+            if (y < g.H[l] && x < g.W[l])
+                st[(g.row0[l] + y * g.W[l] + x) * C + c] = pack_value<T>(dst[c * dw * dw + k], tf32);
+        }
+        src = dst;
+    }
+}
+
+template <typename Tin, typename T>
+int launch_store_t(dc_ctx* ctx, const void* fmaps, int first, int count, cudaStream_t s) {
+    dc::Geom g = dc::geom_of(ctx);
+    dim3 grid((g.w + 7) / 8, (g.h + 7) / 8, count);
+    size_t smem = (size_t)g.C * (64 + 16 + 4 + 1) * sizeof(float);
+    auto k = store_pack_kernel<Tin, T>;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    k<<<grid, 256, smem, s>>>((const Tin*)fmaps, (T*)ctx->store, g, first,
+                              ctx->cfg.precision == DC_PREC_TF32);
+    return dc_check_launch(ctx, "store_pack_kernel");
+}
+
+}  // namespace
+
+int dc_launch_store(dc_ctx* ctx, const void* fmaps, int dtype, int first, int count,
+                    cudaStream_t s) {
+    const int p = ctx->cfg.precision;
+    if (dtype == DC_DTYPE_F32) {
+        if (p == DC_PREC_FP16) return launch_store_t<float, __half>(ctx, fmaps, first, count, s);
+        if (p == DC_PREC_BF16) return launch_store_t<float, __nv_bfloat16>(ctx, fmaps, first, count, s);
+        return launch_store_t<float, float>(ctx, fmaps, first, count, s);
+    }
+    if (p == DC_PREC_FP16) return launch_store_t<__half, __half>(ctx, fmaps, first, count, s);
+    if (p == DC_PREC_BF16) return launch_store_t<__half, __nv_bfloat16>(ctx, fmaps, first, count, s);
+    return launch_store_t<__half, float>(ctx, fmaps, first, count, s);
+}

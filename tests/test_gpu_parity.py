@@ -1,0 +1,264 @@
+"""GPU parity of libdroidcorr against the CPU oracle and the reference kernels.
+
+Bars (stated per test):
+  - lookup and pooling: bit-exact (same volumes in, same bits out);
+  - fp32 exact-FFMA volume build: bit-exact against the oracle's fmaf chain;
+  - fp32 fused / alt-corr: normwise max|a-b| / max|ref| <= 1e-5 against the
+    fp64-accumulating oracle;
+  - fp16 / bf16 / tf32 (tensor-core precisions): normwise <= 2e-2 against the
+    oracle on the same rounded inputs, max-abs error printed.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from slam_hands_b200 import DroidCorrelation, DroidCorrError, configs
+from oracle import ref as REF
+
+pytestmark = pytest.mark.gpu
+
+TOL_FP32 = 1e-5
+TOL_LOW = 2e-2
+
+
+def normwise(a, b):
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+def setup(h, w, K=3, C=128, seed=0, sigma=2.0, M=2, precision="fp32", alpha=1 / 16, **kw):
+    rng = np.random.default_rng(seed)
+    fm = rng.standard_normal((K, C, h, w), dtype=np.float32)
+    ii = rng.integers(0, K, M).astype(np.int32)
+    jj = ((ii + 1 + rng.integers(0, K - 1, M)) % K).astype(np.int32)
+    coords = (configs.grid_coords(h, w)[None] + rng.normal(0, sigma, (M, 2, h, w))).astype(np.float32)
+    dc = DroidCorrelation(h, w, channels=C, precision=precision, alpha=alpha,
+                          max_frames=max(K, 4), **kw)
+    dc.set_frames(torch.from_numpy(fm).cuda())
+    return dc, fm, ii, jj, coords
+
+
+def round_like(x, precision):
+    if precision == "fp16":
+        return x.astype(np.float16).astype(np.float32)
+    if precision == "bf16":
+        return torch.from_numpy(x).to(torch.bfloat16).float().numpy()
+    if precision == "tf32":
+        # round to nearest, ties away from zero, 10 mantissa bits (cvt.rna.tf32.f32)
+        b = x.view(np.uint32).astype(np.uint64)
+        b = (b + 0x1000) & 0xFFFFE000
+        return b.astype(np.uint32).view(np.float32)
+    return x
+
+
+def oracle_alt(oracle, fm, ii, jj, coords, alpha, precision, levels=4, radius=3):
+    """Expected output of the fused / alt paths: the pooled target pyramid in
+    fp32, rounded like the store, dot products in double."""
+    M = len(ii)
+    h, w = fm.shape[-2:]
+    D = 2 * radius + 1
+    out = np.empty((M, levels * D * D, h, w), np.float32)
+    for e in range(M):
+        fi = round_like(fm[ii[e]], precision)
+        pyr = [round_like(p, precision) for p in oracle.fmap_pyramid(fm[jj[e]], levels)]
+        C = fi.shape[0]
+        import ctypes
+        from oracle.oracle import _f, _fp, lib
+        pyr = [np.ascontiguousarray(p.reshape(C, -1)) for p in pyr]
+        arr = (_fp * levels)(*[_f(p) for p in pyr])
+        fi = np.ascontiguousarray(fi.reshape(C, -1))
+        o = np.empty((levels * D * D, h, w), np.float32)
+        assert lib().orc_alt_lookup_edge(_f(fi), arr, levels, C, _f(coords[e]), _f(o), h, w,
+                                         radius, float(alpha)) == 0
+        out[e] = o
+    return out
+
+
+# ---------------------------------------------------------------- lookup / pool
+
+@pytest.mark.parametrize("h,w", [(48, 64), (41, 73), (5, 9), (54, 96)])
+def test_lookup_bit_exact_vs_oracle(cuda, oracle, h, w):
+    M = 3 if h * w <= 3072 else 1
+    rng = np.random.default_rng(h * w)
+    levels = 4 if min(h, w) >= 8 else 1
+    vols = [rng.standard_normal((M, h * w, h >> l, w >> l), dtype=np.float32) for l in range(levels)]
+    coords = (configs.grid_coords(h, w)[None] + rng.uniform(-6, 6, (M, 2, h, w))).astype(np.float32)
+    coords[:, :, 0, :3] = -0.5        # negative fractional
+    coords[:, :, 1, :3] = 3.0         # integer
+    coords[:, :, 2, :3] = -1000.0     # all out of bounds
+    dc = DroidCorrelation(h, w, levels=levels, max_frames=1)
+    out = dc.lookup([torch.from_numpy(v).cuda() for v in vols], torch.from_numpy(coords).cuda())
+    ref = oracle.lookup(vols, coords, h, w, 3)
+    assert np.array_equal(out.cpu().numpy(), ref)
+
+
+def test_lookup_single_bit_exact_vs_oracle(cuda, oracle):
+    h, w = 48, 64
+    rng = np.random.default_rng(11)
+    vols = [rng.standard_normal((1, h * w, h >> l, w >> l), dtype=np.float32) for l in range(4)]
+    coords = (configs.grid_coords(h, w)[None] + rng.uniform(-4, 4, (1, 2, h, w))).astype(np.float32)
+    dc = DroidCorrelation(h, w, max_frames=1)
+    out = dc.lookup_single([torch.from_numpy(v[0]).cuda() for v in vols],
+                           torch.from_numpy(coords[0]).cuda())
+    ref = oracle.lookup(vols, coords, h, w, 3, oracle.LOOKUP_SINGLE)[0]
+    assert np.array_equal(out.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("N,H,W", [(1000, 48, 64), (300, 41, 73), (7, 5, 9), (5, 1, 8)])
+def test_pool_bit_exact(cuda, oracle, N, H, W):
+    import ctypes
+    from slam_hands_b200 import _lib as L
+    x = np.random.default_rng(N).standard_normal((N, H, W), dtype=np.float32)
+    xt = torch.from_numpy(x).cuda()
+    out = torch.full((N, H // 2, W // 2), float("nan"), device="cuda")
+    rc = L.load().dc_pool_2x2(xt.data_ptr(), out.data_ptr(), N, H, W,
+                              torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy(), oracle.pool2x2(x))
+
+
+# ---------------------------------------------------------------- volume build
+
+@pytest.mark.parametrize("h,w", [(48, 64), (41, 73)])
+def test_build_volume_fp32_bit_exact(cuda, oracle, h, w):
+    dc, fm, ii, jj, coords = setup(h, w, precision="fp32", M=2)
+    vols = dc.build_volume(ii, jj)
+    torch.cuda.synchronize()
+    for e in range(2):
+        V = oracle.volume_f32_chain(fm[ii[e]], fm[jj[e]], 1 / 16)
+        assert np.array_equal(vols[0][e].cpu().numpy().reshape(h * w, h * w), V)
+        pyr = oracle.pyramid(V, h, w, 4)
+        for l in range(1, 4):
+            assert np.array_equal(vols[l][e].cpu().numpy(), pyr[l])
+
+
+@pytest.mark.parametrize("precision", ["fp16", "bf16", "tf32"])
+def test_build_volume_low_precision(cuda, oracle, precision):
+    h, w = 48, 64
+    dc, fm, ii, jj, coords = setup(h, w, precision=precision, M=2)
+    vols = dc.build_volume(ii, jj)
+    for e in range(2):
+        V = oracle.volume_f64(round_like(fm[ii[e]], precision), round_like(fm[jj[e]], precision), 1 / 16)
+        got = vols[0][e].cpu().numpy().reshape(h * w, h * w)
+        err = normwise(got, V)
+        print(f"{precision} build normwise {err:.3e} maxabs {np.abs(got - V).max():.3e}")
+        assert err < TOL_LOW
+        # the exact-product FFMA path is in fact fp32-accurate on rounded inputs
+        assert err < 1e-5
+
+
+# ---------------------------------------------------------------- fused / alt
+
+@pytest.mark.parametrize("precision,tol", [("fp32", TOL_FP32), ("fp16", TOL_LOW),
+                                           ("bf16", TOL_LOW), ("tf32", TOL_LOW)])
+@pytest.mark.parametrize("entry", ["build_and_lookup", "alt_lookup"])
+def test_fused_and_alt_vs_oracle(cuda, oracle, precision, tol, entry):
+    h, w = 48, 64
+    alpha = 1 / math.sqrt(128)
+    dc, fm, ii, jj, coords = setup(h, w, precision=precision, M=3, sigma=4.0, alpha=alpha)
+    out = getattr(dc, entry)(ii, jj, torch.from_numpy(coords).cuda()).cpu().numpy()
+    exp = oracle_alt(oracle, fm, ii, jj, coords, alpha, precision)
+    err = normwise(out, exp)
+    print(f"{entry} {precision}: normwise {err:.3e} maxabs {np.abs(out - exp).max():.3e}")
+    assert err < (tol if precision == "fp32" else 1e-5)
+    # against the unrounded fp64 materialised pipeline (the reference's math)
+    if precision != "fp32":
+        ref = oracle_alt(oracle, fm, ii, jj, coords, alpha, "fp32")
+        assert normwise(out, ref) < tol
+
+
+def test_fused_equals_materialised_pipeline(cuda, oracle):
+    # dc_build_and_lookup == dc_build_volume + dc_lookup (linearity), fp32
+    h, w = 41, 73
+    dc, fm, ii, jj, coords = setup(h, w, precision="fp32", M=2, sigma=3.0)
+    c = torch.from_numpy(coords).cuda()
+    fused = dc.build_and_lookup(ii, jj, c).cpu().numpy()
+    mat = dc.lookup(dc.build_volume(ii, jj), c).cpu().numpy()
+    assert normwise(fused, mat) < TOL_FP32
+
+
+def test_chunking_and_empty_batch(cuda, oracle):
+    h, w = 12, 16
+    dc, fm, ii, jj, coords = setup(h, w, K=4, precision="fp32", M=7, max_edges=3)
+    c = torch.from_numpy(coords).cuda()
+    out = dc.build_and_lookup(ii, jj, c).cpu().numpy()
+    exp = oracle_alt(oracle, fm, ii, jj, coords, 1 / 16, "fp32")
+    assert normwise(out, exp) < TOL_FP32
+    empty = dc.build_and_lookup(ii[:0], jj[:0], c[:0])
+    assert empty.shape == (0, 196, h, w)
+
+
+def test_errors_are_statuses(cuda):
+    dc = DroidCorrelation(12, 16, max_frames=2, max_edges=2)
+    with pytest.raises(DroidCorrError):
+        dc.set_frames(torch.zeros(3, 128, 12, 16, device="cuda"), first_slot=0)  # 3 > max_frames
+    import ctypes
+    lib = dc.lib
+    c = torch.zeros(3, 2, 12, 16, device="cuda")
+    o = torch.zeros(3, 196, 12, 16, device="cuda")
+    e = torch.zeros(3, dtype=torch.int32, device="cuda")
+    rc = lib.dc_build_and_lookup(dc._ctx, e.data_ptr(), e.data_ptr(), 3, c.data_ptr(),
+                                 o.data_ptr(), None)
+    assert rc == 1 and b"max_edges" in lib.dc_last_error(dc._ctx)
+
+
+def test_set_frames_fp16_input(cuda, oracle):
+    # reference fmaps are __half (main.cu:677): fp16 input is accepted as is
+    h, w = 12, 16
+    rng = np.random.default_rng(12)
+    fm = rng.standard_normal((2, 128, h, w)).astype(np.float16)
+    dc = DroidCorrelation(h, w, precision="fp16", max_frames=2)
+    dc.set_frames(torch.from_numpy(fm).cuda())
+    coords = (configs.grid_coords(h, w)[None] + rng.normal(0, 2, (1, 2, h, w))).astype(np.float32)
+    out = dc.build_and_lookup([0], [1], torch.from_numpy(coords).cuda()).cpu().numpy()
+    exp = oracle_alt(oracle, fm.astype(np.float32), [0], [1], coords, 1 / 16, "fp16")
+    assert normwise(out, exp) < 1e-5
+
+
+# ---------------------------------------------------------------- reference kernels
+
+needs_ref = pytest.mark.skipif(not REF.available(), reason="oracle/_ref not built")
+
+
+@needs_ref
+def test_reference_kernels_pin_the_oracle(cuda, oracle):
+    # the oracle's lookup and pool are bit-identical to the reference's own kernels
+    h, w = 48, 64
+    rng = np.random.default_rng(21)
+    vols = [rng.standard_normal((2, h * w, h >> l, w >> l), dtype=np.float32) for l in range(4)]
+    coords = (configs.grid_coords(h, w)[None] + rng.uniform(-4, 4, (2, 2, h, w))).astype(np.float32)
+    assert np.array_equal(REF.lookup_batched(vols, coords, h, w), oracle.lookup(vols, coords, h, w, 3))
+    assert np.array_equal(REF.lookup_single([v[0] for v in vols], coords[0], h, w),
+                          oracle.lookup([v[:1] for v in vols], coords[:1], h, w, 3,
+                                        oracle.LOOKUP_SINGLE)[0])
+    assert np.array_equal(REF.pool(vols[0]), oracle.pool2x2(vols[0]))
+
+
+@needs_ref
+def test_library_vs_reference_kernels(cuda):
+    # same volumes -> libdroidcorr lookup == reference batch_corr_sample_kernel, bit for bit
+    h, w = 41, 73
+    rng = np.random.default_rng(22)
+    vols = [rng.standard_normal((2, h * w, h >> l, w >> l), dtype=np.float32) for l in range(4)]
+    coords = (configs.grid_coords(h, w)[None] + rng.normal(0, 3, (2, 2, h, w))).astype(np.float32)
+    dc = DroidCorrelation(h, w, max_frames=1)
+    out = dc.lookup([torch.from_numpy(v).cuda() for v in vols], torch.from_numpy(coords).cuda())
+    assert np.array_equal(out.cpu().numpy(), REF.lookup_batched(vols, coords, h, w))
+
+
+@needs_ref
+def test_full_path_vs_reference_fp16(cuda, oracle):
+    # the reference pipeline (FP16 fmaps, cublasGemmBatchedEx, pools, lookups) vs the fused path
+    wl = configs.WORKLOADS["C2"]
+    fm = configs.make_fmaps_np(wl)
+    ii, jj = configs.make_edges(wl)
+    coords = configs.make_coords_np(wl, len(ii))
+    ref_out, _, _ = REF.build_and_sample_fp16(fm, ii, jj, coords, wl.alpha)
+    dc = DroidCorrelation(wl.h, wl.w, precision="fp16", alpha=wl.alpha, max_frames=wl.frames)
+    dc.set_frames(torch.from_numpy(fm).cuda())
+    out = dc.build_and_lookup(ii, jj, torch.from_numpy(coords).cuda()).cpu().numpy()
+    err = normwise(out, ref_out)
+    print(f"fused fp16 vs reference: normwise {err:.3e} maxabs {np.abs(out - ref_out).max():.3e}")
+    assert err < TOL_LOW
