@@ -151,6 +151,11 @@ int dc_build_and_lookup(dc_ctx* ctx, const int* ii_dev, const int* jj_dev, int M
 int dc_alt_lookup(dc_ctx* ctx, const int* ii_dev, const int* jj_dev, int M,
                   const float* coords_dev, float* out_dev, dc_stream_t stream);
 
+/* Wait for `stream`, then report and clear the device error word that the
+ * library's bounded device-side waits raise when they time out: DC_OK or
+ * DC_ERR_DEVICE_TIMEOUT.  (The reference has no device-side waits.) */
+int dc_device_status(dc_ctx* ctx, dc_stream_t stream);
+
 /* Number of kernel launches the library has issued on this context (for
  * launch accounting in benchmarks). */
 long long dc_launch_count(const dc_ctx* ctx);

@@ -61,6 +61,7 @@ SIGNATURES = {
     "dc_build_and_lookup": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp]),
     "dc_alt_lookup": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp]),
     "dc_launch_count": (_ll, [_vp]),
+    "dc_device_status": (_i, [_vp, _vp]),
 }
 
 _lib = None

@@ -105,6 +105,22 @@ int dc_create(const dc_config* cfg, dc_ctx** out) {
         delete ctx;
         return DC_ERR_CUDA;
     }
+    if (cudaMalloc(&ctx->dev_err, sizeof(int)) != cudaSuccess ||
+        cudaMemset(ctx->dev_err, 0, sizeof(int)) != cudaSuccess) {
+        cudaFree(ctx->store);
+        delete ctx;
+        return DC_ERR_NO_MEMORY;
+    }
+    if (dc_tc_supported(ctx)) {
+        int rc = dc_tc_prepare(ctx);
+        if (rc != DC_OK) {
+            cudaFree(ctx->dev_err);
+            cudaFree(ctx->store);
+            delete ctx;
+            return rc;
+        }
+    }
+    cudaDeviceSynchronize();
     *out = ctx;
     return DC_OK;
 }
@@ -115,6 +131,7 @@ int dc_destroy(dc_ctx* ctx) {
     cudaGetDevice(&prev);
     cudaSetDevice(ctx->device);
     if (ctx->store) cudaFree(ctx->store);
+    if (ctx->dev_err) cudaFree(ctx->dev_err);
     if (prev >= 0) cudaSetDevice(prev);
     delete ctx;
     return DC_OK;
@@ -184,6 +201,7 @@ int dc_build_and_lookup(dc_ctx* ctx, const int* ii, const int* jj, int M, const 
     if (rc) return rc;
     if (M == 0) return DC_OK;
     if (!coords || !out) return dc_fail(ctx, DC_ERR_INVALID_ARG, "NULL pointer");
+    if (ctx->tc_ready) return dc_launch_tc(ctx, ii, jj, M, coords, out, (cudaStream_t)stream);
     return dc_launch_alt(ctx, ii, jj, M, coords, out, (cudaStream_t)stream);
 }
 
@@ -195,6 +213,21 @@ int dc_alt_lookup(dc_ctx* ctx, const int* ii, const int* jj, int M, const float*
     if (M == 0) return DC_OK;
     if (!coords || !out) return dc_fail(ctx, DC_ERR_INVALID_ARG, "NULL pointer");
     return dc_launch_alt(ctx, ii, jj, M, coords, out, (cudaStream_t)stream);
+}
+
+int dc_device_status(dc_ctx* ctx, dc_stream_t stream) {
+    if (!ctx) return DC_ERR_INVALID_ARG;
+    if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess)
+        return dc_fail(ctx, DC_ERR_CUDA, cudaGetErrorString(cudaGetLastError()));
+    int v = 0;
+    if (cudaMemcpy(&v, ctx->dev_err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+        return dc_fail(ctx, DC_ERR_CUDA, "reading the device error word failed");
+    if (v != 0) {
+        cudaMemset(ctx->dev_err, 0, sizeof(int));
+        return dc_fail(ctx, DC_ERR_DEVICE_TIMEOUT,
+                       "a device-side wait timed out (site " + std::to_string(v) + ")");
+    }
+    return DC_OK;
 }
 
 }  // extern "C"

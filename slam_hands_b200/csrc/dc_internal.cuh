@@ -34,6 +34,11 @@ struct dc_ctx {
     long long store_bytes = 0;
     int num_sms = 148;
     long long launches = 0;
+    int* dev_err = nullptr;  // device error word raised by bounded device waits
+    // tensor maps of the store for the tensor-core kernel (CUtensorMap storage)
+    alignas(64) unsigned char tmap_a[128];
+    alignas(64) unsigned char tmap_b[128];
+    bool tc_ready = false;
     std::string err;
 };
 
@@ -121,5 +126,9 @@ int dc_launch_pool2x2(const float* in, float* out, long long N, int H, int W,
                       cudaStream_t s);
 int dc_launch_lookup(dc_ctx* ctx, const float* const* vols, const float* coords, float* out,
                      int M, bool single_edge_arith, cudaStream_t s);
+bool dc_tc_supported(const dc_ctx* ctx);
+int dc_tc_prepare(dc_ctx* ctx);
+int dc_launch_tc(dc_ctx* ctx, const int* ii, const int* jj, int M, const float* coords,
+                 float* out, cudaStream_t s);
 int dc_launch_alt(dc_ctx* ctx, const int* ii, const int* jj, int M, const float* coords,
                   float* out, cudaStream_t s);

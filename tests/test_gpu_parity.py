@@ -151,22 +151,40 @@ def test_build_volume_low_precision(cuda, oracle, precision):
 
 # ---------------------------------------------------------------- fused / alt
 
-@pytest.mark.parametrize("precision,tol", [("fp32", TOL_FP32), ("fp16", TOL_LOW),
-                                           ("bf16", TOL_LOW), ("tf32", TOL_LOW)])
+@pytest.mark.parametrize("precision", ["fp32", "fp16", "bf16", "tf32"])
 @pytest.mark.parametrize("entry", ["build_and_lookup", "alt_lookup"])
-def test_fused_and_alt_vs_oracle(cuda, oracle, precision, tol, entry):
-    h, w = 48, 64
+@pytest.mark.parametrize("h,w,sigma", [(48, 64, 4.0), (41, 73, 8.0), (54, 96, 3.0)])
+def test_fused_and_alt_vs_oracle(cuda, oracle, precision, entry, h, w, sigma):
     alpha = 1 / math.sqrt(128)
-    dc, fm, ii, jj, coords = setup(h, w, precision=precision, M=3, sigma=4.0, alpha=alpha)
+    dc, fm, ii, jj, coords = setup(h, w, precision=precision, M=2, sigma=sigma, alpha=alpha)
     out = getattr(dc, entry)(ii, jj, torch.from_numpy(coords).cuda()).cpu().numpy()
+    assert dc.lib.dc_device_status(dc._ctx, None) == 0
     exp = oracle_alt(oracle, fm, ii, jj, coords, alpha, precision)
     err = normwise(out, exp)
-    print(f"{entry} {precision}: normwise {err:.3e} maxabs {np.abs(out - exp).max():.3e}")
-    assert err < (tol if precision == "fp32" else 1e-5)
-    # against the unrounded fp64 materialised pipeline (the reference's math)
+    print(f"{entry} {precision} {h}x{w}: normwise {err:.3e} maxabs {np.abs(out - exp).max():.3e}")
+    tensor_path = entry == "build_and_lookup" and precision in ("fp16", "bf16")
+    # same rounded operands: the FFMA paths are fp32-exact; tensor-core
+    # accumulation order differs, still far below the 2e-2 bar
+    assert err < (1e-4 if tensor_path else TOL_FP32)
     if precision != "fp32":
+        # against the unrounded pipeline (the reference's math on fp32 inputs)
         ref = oracle_alt(oracle, fm, ii, jj, coords, alpha, "fp32")
-        assert normwise(out, ref) < tol
+        err2 = normwise(out, ref)
+        print(f"   vs fp32 inputs: normwise {err2:.3e} maxabs {np.abs(out - ref).max():.3e}")
+        assert err2 < TOL_LOW
+
+
+@pytest.mark.parametrize("C", [64, 128])
+def test_tensor_path_channels_and_extreme_coords(cuda, oracle, C):
+    h, w = 48, 64
+    dc, fm, ii, jj, coords = setup(h, w, C=C, precision="fp16", M=3, sigma=20.0)
+    coords[0] = -50.0                  # edge 0: every window outside
+    coords[1, :, :10] = 1e4            # edge 1: some pixels far outside
+    out = dc.build_and_lookup(ii, jj, torch.from_numpy(coords).cuda()).cpu().numpy()
+    assert dc.lib.dc_device_status(dc._ctx, None) == 0
+    exp = oracle_alt(oracle, fm, ii, jj, coords, 1 / 16, "fp16")
+    assert np.all(out[0] == 0.0)
+    assert normwise(out, exp) < 1e-4
 
 
 def test_fused_equals_materialised_pipeline(cuda, oracle):
