@@ -35,9 +35,8 @@ struct dc_ctx {
     int num_sms = 148;
     long long launches = 0;
     int* dev_err = nullptr;  // device error word raised by bounded device waits
-    // tensor maps of the store for the tensor-core kernel (CUtensorMap storage)
+    // tensor map of the store for the tensor-core kernel (CUtensorMap storage)
     alignas(64) unsigned char tmap_a[128];
-    alignas(64) unsigned char tmap_b[128];
     bool tc_ready = false;
     std::string err;
 };

@@ -8,20 +8,23 @@
 //   1. reduces, over its 128 pixels, the range of target rows any window of
 //      level l touches (so only those rows of the level are correlated);
 //   2. streams those rows of the pooled target map P_l f_jj (pixel-major store,
-//      K-major operand) through shared memory with TMA, 256 target pixels per
-//      chunk, double-buffered;
-//   3. computes the 128 x 256 x C correlation chunk with tcgen05.mma (kind::f16,
-//      fp16 or bf16 operands, fp32 accumulation in TMEM, two accumulators so the
-//      epilogue of chunk c overlaps the MMAs of chunk c+1);
-//   4. reads back only the 32-column TMEM slices that hold some pixel's window
-//      taps (tcgen05.ld), picks each pixel's taps into its window in shared
-//      memory, and after the last chunk of a level forms the (2r+1)^2 bilinear
-//      outputs in the reference's rounding order (main.cu:1196-1213) and stores
-//      them with coalesced 128-byte rows of out[e][l*(2r+1)^2 + a*(2r+1) + b][p].
+//      K-major operand) through shared memory with TMA in row-aligned chunks of
+//      at most 128 target pixels, double-buffered;
+//   3. computes each 128 x n x C correlation chunk with tcgen05.mma (kind::f16,
+//      fp16 or bf16 operands, fp32 accumulation in TMEM, four accumulators so the
+//      epilogue of chunk c overlaps the MMAs of the next chunks);
+//   4. reads back only the TMEM columns that hold some pixel's window taps
+//      (tcgen05.ld), stages the 16-byte groups a pixel needs in shared memory,
+//      picks its taps into its window, and after the last chunk of a level forms
+//      the (2r+1)^2 bilinear outputs in the reference's rounding order
+//      (main.cu:1196-1213), stored as coalesced 128-byte rows of
+//      out[e][l*(2r+1)^2 + a*(2r+1) + b][p].
 //
-// Warp roles (192 threads): warp 0 issues TMA, warp 1 allocates TMEM and issues
-// MMAs (one elected lane each), warps 2..5 are the epilogue; warp w reads TMEM
-// lanes 32*(w%4) .. 32*(w%4)+31, i.e. tile pixels 32*(w%4) + lane.
+// Warp roles (320 threads): warp 0 issues TMA, warp 1 allocates TMEM and issues
+// MMAs (one elected lane each), warps 2..9 are the epilogue.  Warp w reads TMEM
+// lanes 32*(w%4) .. 32*(w%4)+31, i.e. tile pixels 32*(w%4) + lane; the two warps
+// of a lane quarter take the two 64-column halves of a chunk and split the
+// outputs.
 //
 // Every mbarrier wait is bounded (2 s); on a time-out the CTA raises the
 // context's device error word, stops all roles, waits (bounded) for its TMA
@@ -36,16 +39,24 @@ namespace {
 using namespace dc::sm100;
 
 constexpr int kTileM = 128;      // source pixels per CTA = MMA M = TMEM lanes
-constexpr int kChunkN = 256;     // target pixels per chunk = MMA N (max)
-constexpr int kThreads = 192;
-constexpr int kMaxChunks = 128;
+constexpr int kChunkN = 128;     // max target pixels per chunk = MMA N
+constexpr int kHalfCols = 64;    // chunk columns per epilogue warp
+constexpr int kStagesB = 2;      // shared-memory stages of target rows
+constexpr int kAcc = 4;          // TMEM accumulators (kAcc * kChunkN = 512 columns)
+constexpr int kEpiWarps = 8;     // two warps per TMEM lane quarter
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kMaxChunks = 256;
 constexpr int kWinStride = 65;   // floats per pixel window row (64 taps + pad)
-constexpr int kStStride = 33;    // floats per staged TMEM row (32 + pad)
-constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kAtomRowsBytes = 128;  // one 128-byte K atom per row
+constexpr int kStStride = kHalfCols + 4;  // floats per staged TMEM row (16-byte rows)
+constexpr uint32_t kTmemCols = kAcc * kChunkN;
+constexpr uint32_t kRowBytes = 128;  // one 128-byte K atom per operand row
 
+// A chunk is `nrows` consecutive target rows of one level, each the segment
+// [x0, x0 + seg) of the row (seg = W when whole rows fit, else a row is split).
 struct ChunkDesc {
-    int level, q0, n, row;
+    int level, n, row;     // MMA N (multiple of 16), store row of the first pixel
+    int y0, x0, seg;       // level coordinates of chunk column 0, segment length
+    int rlo[2], rhi[2];    // chunk rows touched by columns [64h, 64h + 64), h = 0, 1
 };
 
 struct TcParams {
@@ -64,44 +75,72 @@ struct Layout {
     uint32_t a, b, stage_b, win, st, chunks, bars, misc, total;
 };
 
-__host__ __device__ inline Layout make_layout(int atoms) {
-    Layout L;
+__host__ __device__ constexpr Layout make_layout(int atoms) {
+    Layout L{};
     L.a = 0;
-    L.b = L.a + atoms * kTileM * kAtomRowsBytes;
-    L.stage_b = atoms * kChunkN * kAtomRowsBytes;
-    L.win = L.b + 2 * L.stage_b;
+    L.b = L.a + atoms * kTileM * kRowBytes;
+    L.stage_b = atoms * kChunkN * kRowBytes;
+    L.win = L.b + kStagesB * L.stage_b;
     L.st = L.win + kTileM * kWinStride * 4;
-    L.chunks = L.st + kTileM * kStStride * 4;
+    L.chunks = L.st + kEpiWarps * 32 * kStStride * 4;
     L.bars = L.chunks + kMaxChunks * sizeof(ChunkDesc);
     L.misc = L.bars + 16 * 8;
     L.total = L.misc + 64;
     return L;
 }
+static_assert(make_layout(2).total + 1024 <= 227 * 1024, "shared memory budget");
 
 // misc words
 enum { kMiscTmem = 0, kMiscAbort = 1, kMiscCount = 2, kMiscRange = 4 };  // range: 2 per level
 // barrier slots
-enum { kBarA = 0, kBarFull = 1, kBarEmpty = 3, kBarTFull = 5, kBarTEmpty = 7 };
+enum { kBarA = 0, kBarFull = 1, kBarEmpty = kBarFull + kStagesB,
+       kBarTFull = kBarEmpty + kStagesB, kBarTEmpty = kBarTFull + kAcc };
+static_assert(kBarTEmpty + kAcc <= 16, "barrier slots");
 
 __device__ __forceinline__ void raise_abort(volatile int* abort, int* err, int code) {
     *abort = 1;
     atomicExch(err, code);
 }
 
+// Optional phase timers (build with -DDC_TC_PROFILE; compiled out otherwise):
+// per CTA, cycles spent in set-up, in each role's waits and in the epilogue
+// phases, for tuning the pipeline.
+#ifdef DC_TC_PROFILE
+__device__ unsigned long long g_tc_prof[8192 * 16];
+#define DC_PROF_NOW() clock64()
+#define DC_PROF_STORE(slot, v)                                                    \
+    do {                                                                          \
+        const int cta_ = blockIdx.y * gridDim.x + blockIdx.x;                     \
+        if (cta_ < 8192) g_tc_prof[cta_ * 16 + (slot)] = (unsigned long long)(v); \
+    } while (0)
+#else
+#define DC_PROF_NOW() 0ll
+#define DC_PROF_STORE(slot, v) \
+    do {                       \
+    } while (0)
+#endif
+
+__device__ __forceinline__ void pair_sync(int quarter) {
+    asm volatile("bar.sync %0, %1;" ::"r"(1 + quarter), "r"(64) : "memory");
+}
+
 template <int R>
 __global__ void __launch_bounds__(kThreads, 1)
-    corr_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                   const __grid_constant__ CUtensorMap tmap_b, TcParams P) {
+    corr_tc_kernel(const __grid_constant__ CUtensorMap tmap, TcParams P) {
     constexpr int D = 2 * R + 1, NW = 2 * R + 2;
+    constexpr int ASPLIT = (D + 1) / 2;  // epilogue half 0 forms outputs a < ASPLIT
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const Layout Ly = make_layout(P.atoms);
+    constexpr Layout Ly2 = make_layout(2);
+    const Layout Ly = P.atoms == 2 ? Ly2 : make_layout(P.atoms);
     const dc::Geom& g = P.g;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int e = blockIdx.y, p0 = blockIdx.x * kTileM;
     const int hw = g.hw, nch = g.levels * D * D;
     float* out_e = P.out + (size_t)e * nch * hw;
+    const long long t_start = DC_PROF_NOW();
+    (void)t_start;
 
     const int si = P.ii[e], sj = P.jj[e];
     if (!(si >= 0 && si < P.max_frames && sj >= 0 && sj < P.max_frames)) {
@@ -122,13 +161,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int* abort = misc + kMiscAbort;
     auto bar = [&](int slot) { return bars + 8u * slot; };
 
+    const bool epi = warp >= 2;
+    const int quarter = warp & 3;            // TMEM lane quarter of this warp
+    const int half = (warp - 2) >> 2;        // 0: warps 2-5, 1: warps 6-9
+    const int ti = 32 * quarter + lane;      // tile pixel (epilogue threads)
+    const int p = p0 + ti;
+    const bool pv = epi && p < hw;
+    float cx = 0.0f, cy = 0.0f;
+    if (pv) {
+        cx = __ldg(P.coords + (size_t)e * 2 * hw + p);
+        cy = __ldg(P.coords + (size_t)e * 2 * hw + hw + p);
+    }
+
     if (threadIdx.x == 0) {
         mbar_init(bar(kBarA), 1);
-        for (int s = 0; s < 2; s++) {
+        for (int s = 0; s < kStagesB; s++) {
             mbar_init(bar(kBarFull + s), 1);
             mbar_init(bar(kBarEmpty + s), 1);
-            mbar_init(bar(kBarTFull + s), 1);
-            mbar_init(bar(kBarTEmpty + s), 4);
+        }
+        for (int a = 0; a < kAcc; a++) {
+            mbar_init(bar(kBarTFull + a), 1);
+            mbar_init(bar(kBarTEmpty + a), kEpiWarps);
         }
         misc[kMiscAbort] = 0;
         for (int l = 0; l < DC_MAX_LEVELS; l++) {
@@ -136,8 +189,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             misc[kMiscRange + 2 * l + 1] = -1;
         }
         fence_mbar_init();
-        tma_prefetch_desc(&tmap_a);
-        tma_prefetch_desc(&tmap_b);
+        tma_prefetch_desc(&tmap);
     }
     if (warp == 1) {
         tmem_alloc(smem_addr(misc + kMiscTmem), kTmemCols);
@@ -148,19 +200,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = (uint32_t)misc[kMiscTmem];
 
+    // the source tile does not depend on the windows: start its load now
+    if (threadIdx.x == 0) {
+        mbar_arrive_expect_tx(bar(kBarA), P.atoms * kTileM * kRowBytes);
+        const int arow = (int)((long long)si * g.frame_rows + g.row0[0] + p0);
+        for (int k = 0; k < P.atoms; k++)
+            tma_load_2d(sA + k * kTileM * kRowBytes, &tmap, k * 64, arow, bar(kBarA));
+    }
+
     // ---- 1. target-row range per level over this tile's windows
-    const bool epi = warp >= 2;
-    const int ti = 32 * (warp & 3) + lane;  // tile pixel (epilogue threads)
-    const int p = p0 + ti;
-    const bool pv = epi && p < hw;
-    float cx = 0.0f, cy = 0.0f;
-    if (pv) {
-        cx = __ldg(P.coords + (size_t)e * 2 * hw + p);
-        cy = __ldg(P.coords + (size_t)e * 2 * hw + hw + p);
+    if (pv && half == 0) {
         for (int l = 0; l < g.levels; l++) {
-            const float y0 = cy * (1.0f / (float)(1 << l));
-            const float x0 = cx * (1.0f / (float)(1 << l));
-            const int by = (int)floorf(y0) - R, bx = (int)floorf(x0) - R;
+            const float sc = 1.0f / (float)(1 << l);
+            const int by = (int)floorf(cy * sc) - R, bx = (int)floorf(cx * sc) - R;
             const int lo = max(by, 0), hi = min(by + NW - 1, g.H[l] - 1);
             const bool xin = bx + NW - 1 >= 0 && bx < g.W[l];
             if (lo <= hi && xin) {
@@ -175,50 +227,66 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int l = 0; l < g.levels; l++) {
             const int ylo = misc[kMiscRange + 2 * l], yhi = misc[kMiscRange + 2 * l + 1];
             if (ylo > yhi) continue;
-            const int qs = ylo * g.W[l], qe = (yhi + 1) * g.W[l];
-            for (int q = qs; q < qe && n < kMaxChunks; q += kChunkN) {
-                const int len = min(kChunkN, qe - q);
-                ChunkDesc c;
-                c.level = l;
-                c.q0 = q;
-                c.n = (len + 15) & ~15;
-                c.row = (int)((long long)sj * g.frame_rows + g.row0[l] + q);
-                chunks[n++] = c;
+            const int Wl = g.W[l];
+            const int rows_per = Wl <= kChunkN ? kChunkN / Wl : 1;
+            const int seg_max = Wl <= kChunkN ? Wl : kChunkN;
+            for (int y = ylo; y <= yhi; y += rows_per) {
+                const int nrows = min(rows_per, yhi - y + 1);
+                for (int x = 0; x < Wl && n < kMaxChunks; x += seg_max) {
+                    ChunkDesc c;
+                    c.level = l;
+                    c.y0 = y;
+                    c.x0 = x;
+                    c.seg = min(seg_max, Wl - x);
+                    const int cols = nrows * c.seg;
+                    c.n = (cols + 15) & ~15;
+                    c.row = (int)((long long)sj * g.frame_rows + g.row0[l] + y * Wl + x);
+                    for (int h = 0; h < 2; h++) {
+                        c.rlo[h] = (h * kHalfCols) / c.seg;
+                        c.rhi[h] = min(cols - 1, h * kHalfCols + kHalfCols - 1) / c.seg;
+                        if (h * kHalfCols >= cols) c.rhi[h] = -1;
+                    }
+                    chunks[n++] = c;
+                }
             }
         }
         misc[kMiscCount] = n;
     }
     __syncthreads();
     const int nchunks = misc[kMiscCount];
+    if (threadIdx.x == 0) {
+        DC_PROF_STORE(1, DC_PROF_NOW() - t_start);
+        DC_PROF_STORE(8, nchunks);
+    }
+    long long w_a = 0, w_b = 0, w_c = 0;  // per-role phase cycles (profiling builds)
 
     if (warp == 0) {
         // ---- 2. TMA producer
         if (lane == 0) {
-            const uint32_t a_bytes = P.atoms * kTileM * kAtomRowsBytes;
             const uint32_t b_bytes = Ly.stage_b;
-            mbar_arrive_expect_tx(bar(kBarA), a_bytes);
-            const int arow = (int)((long long)si * g.frame_rows + g.row0[0] + p0);
-            for (int k = 0; k < P.atoms; k++)
-                tma_load_2d(sA + k * kTileM * kAtomRowsBytes, &tmap_a, k * 64, arow, bar(kBarA));
             int issued = 0;
             for (int c = 0; c < nchunks; c++) {
-                const int s = c & 1;
-                if (c >= 2 && !mbar_wait(bar(kBarEmpty + s), ((c >> 1) - 1) & 1, abort)) {
+                const int s = c % kStagesB;
+                const long long t0 = DC_PROF_NOW();
+                if (c >= kStagesB &&
+                    !mbar_wait(bar(kBarEmpty + s), ((c / kStagesB) - 1) & 1, abort)) {
                     raise_abort(abort, P.err, 1);
                     break;
                 }
+                w_a += DC_PROF_NOW() - t0;
                 mbar_arrive_expect_tx(bar(kBarFull + s), b_bytes);
-                const ChunkDesc ch = chunks[c];
+                const int row = chunks[c].row;
                 for (int k = 0; k < P.atoms; k++)
-                    tma_load_2d(sB + s * Ly.stage_b + k * kChunkN * kAtomRowsBytes, &tmap_b,
-                                k * 64, ch.row, bar(kBarFull + s));
+                    tma_load_2d(sB + s * Ly.stage_b + k * kChunkN * kRowBytes, &tmap, k * 64, row,
+                                bar(kBarFull + s));
                 issued = c + 1;
             }
+            DC_PROF_STORE(4, w_a);
             if (*abort) {
                 // let this CTA's copies in flight land before the CTA exits
                 mbar_wait(bar(kBarA), 0, nullptr);
-                for (int c = max(0, issued - 2); c < issued; c++)
-                    mbar_wait(bar(kBarFull + (c & 1)), (c >> 1) & 1, nullptr);
+                for (int c = max(0, issued - kStagesB); c < issued; c++)
+                    mbar_wait(bar(kBarFull + c % kStagesB), (c / kStagesB) & 1, nullptr);
             }
         }
         __syncwarp();
@@ -229,39 +297,46 @@ __global__ void __launch_bounds__(kThreads, 1)
                 raise_abort(abort, P.err, 2);
             } else {
                 tc_fence_after();
+                const int ksteps = P.atoms * 4;  // 16 elements (32 bytes) per MMA
                 for (int c = 0; c < nchunks; c++) {
-                    const int s = c & 1, u = c >> 1;
-                    if (!mbar_wait(bar(kBarFull + s), u & 1, abort)) {
+                    const int s = c % kStagesB, a = c % kAcc;
+                    const long long t0 = DC_PROF_NOW();
+                    if (!mbar_wait(bar(kBarFull + s), (c / kStagesB) & 1, abort)) {
                         raise_abort(abort, P.err, 3);
                         break;
                     }
-                    if (c >= 2 && !mbar_wait(bar(kBarTEmpty + s), (u - 1) & 1, abort)) {
+                    const long long t1 = DC_PROF_NOW();
+                    w_a += t1 - t0;
+                    if (c >= kAcc && !mbar_wait(bar(kBarTEmpty + a), ((c / kAcc) - 1) & 1, abort)) {
                         raise_abort(abort, P.err, 4);
                         break;
                     }
+                    w_b += DC_PROF_NOW() - t1;
                     tc_fence_after();
-                    const ChunkDesc ch = chunks[c];
-                    const uint32_t idesc = idesc_f16(P.ab_fmt, kTileM, ch.n);
-                    const uint32_t d = tmem + (uint32_t)(s * kChunkN);
-                    const int ksteps = P.atoms * 4;  // 16 elements (32 bytes) per MMA
+                    const uint32_t idesc = idesc_f16(P.ab_fmt, kTileM, chunks[c].n);
+                    const uint32_t d = tmem + (uint32_t)(a * kChunkN);
                     for (int kk = 0; kk < ksteps; kk++) {
                         const int at = kk >> 2, wi = kk & 3;
-                        const uint64_t ad = sdesc_sw128(sA + at * kTileM * kAtomRowsBytes + wi * 32);
-                        const uint64_t bd = sdesc_sw128(sB + s * Ly.stage_b +
-                                                        at * kChunkN * kAtomRowsBytes + wi * 32);
+                        const uint64_t ad = sdesc_sw128(sA + at * kTileM * kRowBytes + wi * 32);
+                        const uint64_t bd =
+                            sdesc_sw128(sB + s * Ly.stage_b + at * kChunkN * kRowBytes + wi * 32);
                         mma_f16(d, ad, bd, idesc, kk > 0 ? 1u : 0u);
                     }
                     mma_commit(bar(kBarEmpty + s));
-                    mma_commit(bar(kBarTFull + s));
+                    mma_commit(bar(kBarTFull + a));
                 }
+                DC_PROF_STORE(2, w_a);
+                DC_PROF_STORE(3, w_b);
             }
         }
         __syncwarp();
     } else {
-        // ---- 4. epilogue
+        // ---- 4. epilogue: the two warps of a lane quarter take the two
+        //         64-column halves of each chunk
         float* win = win_base + ti * kWinStride;
-        float* st = st_base + ti * kStStride;
-        const uint32_t tl = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
+        float* st = st_base + ((warp - 2) * 32 + lane) * kStStride;
+        const uint32_t tl = tmem + ((uint32_t)(32 * quarter) << 16);
+        const int cbase = kHalfCols * half;
         int c = 0;
         bool alive = true;
         for (int l = 0; l < g.levels && alive; l++) {
@@ -275,47 +350,75 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int xlo = max(bx, 0), xhi = min(bx + NW - 1, Wl - 1);
             const bool any = pv && ylo <= yhi && xlo <= xhi;
             while (c < nchunks && chunks[c].level == l) {
-                const int s = c & 1, u = c >> 1;
+                const int a = c % kAcc;
+                const uint32_t par = (c / kAcc) & 1;
+                const long long t0 = DC_PROF_NOW();
                 int okw = 1;
-                if (lane == 0) okw = mbar_wait(bar(kBarTFull + s), u & 1, abort) ? 1 : 0;
+                if (lane == 0) okw = mbar_wait(bar(kBarTFull + a), par, abort) ? 1 : 0;
                 okw = __shfl_sync(0xffffffffu, okw, 0);
                 if (!okw) {
                     if (lane == 0) raise_abort(abort, P.err, 5);
                     alive = false;
                     break;
                 }
-                mbar_wait(bar(kBarTFull + s), u & 1, abort);
+                mbar_wait(bar(kBarTFull + a), par, abort);
                 tc_fence_after();
-                const ChunkDesc ch = chunks[c];
-                const int nsl = (ch.n + 31) >> 5;
-                for (int t = 0; t < nsl; t++) {
-                    const int qs = ch.q0 + 32 * t, qe = qs + 31;
-                    bool need = false;
-                    if (any) {
-                        const int ya = qs / Wl, yb = qe / Wl;
-                        need = ylo <= yb && yhi >= ya;
-                    }
+                const long long t1 = DC_PROF_NOW();
+                w_a += t1 - t0;
+                const ChunkDesc& ch = chunks[c];
+                const int rlo = half ? ch.rlo[1] : ch.rlo[0];
+                const int rhi = half ? ch.rhi[1] : ch.rhi[0];
+                if (rhi >= 0) {
+                    // window rows of this pixel inside this warp's chunk rows
+                    const int ya = max(ylo, ch.y0 + rlo);
+                    const int yb = min(yhi, ch.y0 + rhi);
+                    // this pixel's taps in staged-column coordinates: row y, tap x
+                    // sits at column (y - y0) * seg + (x - x0) - cbase
+                    const int xa = max(xlo, ch.x0), xb = min(xhi, ch.x0 + ch.seg - 1);
+                    const bool need = any && ya <= yb && xa <= xb;
                     if (__any_sync(0xffffffffu, need)) {
-                        float v[32];
-                        tmem_ld32(tl + (uint32_t)(s * kChunkN + 32 * t), v);
+                        float v[kHalfCols];
+                        tmem_ld64(tl + (uint32_t)(a * kChunkN + cbase), v);
                         if (need) {
+                            const int kofs = -ch.x0 - cbase;
+                            const int klo = max((ya - ch.y0) * ch.seg + xa + kofs, 0);
+                            const int khi = min((yb - ch.y0) * ch.seg + xb + kofs, kHalfCols - 1);
+                            // stage only the 16-byte groups spanning this pixel's taps
+                            float4* st4 = reinterpret_cast<float4*>(st);
 #pragma unroll
-                            for (int k = 0; k < 32; k++) st[k] = v[k];
-                            for (int y = max(ylo, qs / Wl); y <= min(yhi, qe / Wl); y++) {
-                                const int qrow = y * Wl;
-                                const int qa = max(qrow + xlo, qs), qb = min(qrow + xhi, qe);
-                                for (int q = qa; q <= qb; q++)
-                                    win[(q - qrow - bx) * 8 + (y - by)] = g.alpha * st[q - qs];
+                            for (int k = 0; k < kHalfCols / 4; k++)
+                                if (4 * k + 3 >= klo && 4 * k <= khi)
+                                    st4[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2],
+                                                         v[4 * k + 3]);
+                            for (int y = ya; y <= yb; y++) {
+                                const int k0 = (y - ch.y0) * ch.seg + bx + kofs;
+                                float tv[NW];
+#pragma unroll
+                                for (int i = 0; i < NW; i++) {
+                                    const int x = bx + i, k = k0 + i;
+                                    tv[i] = (x >= xa && x <= xb && k >= 0 && k < kHalfCols)
+                                                ? st[k] : 0.0f;
+                                }
+                                float* wcol = win + (y - by);
+#pragma unroll
+                                for (int i = 0; i < NW; i++) {
+                                    const int x = bx + i, k = k0 + i;
+                                    if (x >= xa && x <= xb && k >= 0 && k < kHalfCols)
+                                        wcol[i * 8] = g.alpha * tv[i];
+                                }
                             }
                         }
                     }
                 }
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(bar(kBarTEmpty + s));
+                if (lane == 0) mbar_arrive(bar(kBarTEmpty + a));
                 c++;
+                w_b += DC_PROF_NOW() - t1;
             }
             if (!alive) break;
+            const long long t2 = DC_PROF_NOW();
+            pair_sync(quarter);  // both halves have written this level's windows
             if (pv) {
                 bool vx[NW], vy[NW];
 #pragma unroll
@@ -325,18 +428,34 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 const float ux = 1.0f - dx, uy = 1.0f - dy;
                 float* ol = out_e + (size_t)(l * D * D) * hw + p;
+                const int a0 = half ? ASPLIT : 0, a1 = half ? D : ASPLIT;
+                float tv[NW][NW];
 #pragma unroll
-                for (int a = 0; a < D; a++)
+                for (int i = 0; i < NW; i++)
+#pragma unroll
+                    for (int j = 0; j < NW; j++)
+                        tv[i][j] = (i >= a0 && i <= a1 && vx[i] && vy[j]) ? win[i * 8 + j] : 0.0f;
+#pragma unroll
+                for (int a = 0; a < D; a++) {
+                    if (a < a0 || a >= a1) continue;
 #pragma unroll
                     for (int b = 0; b < D; b++) {
                         float acc = 0.0f;
-                        acc = dc::bilinear_tap(acc, win[a * 8 + b], vx[a] && vy[b], ux, uy);
-                        acc = dc::bilinear_tap(acc, win[a * 8 + b + 1], vx[a] && vy[b + 1], ux, dy);
-                        acc = dc::bilinear_tap(acc, win[(a + 1) * 8 + b], vx[a + 1] && vy[b], dx, uy);
-                        acc = dc::bilinear_tap(acc, win[(a + 1) * 8 + b + 1], vx[a + 1] && vy[b + 1], dx, dy);
+                        acc = dc::bilinear_tap(acc, tv[a][b], vx[a] && vy[b], ux, uy);
+                        acc = dc::bilinear_tap(acc, tv[a][b + 1], vx[a] && vy[b + 1], ux, dy);
+                        acc = dc::bilinear_tap(acc, tv[a + 1][b], vx[a + 1] && vy[b], dx, uy);
+                        acc = dc::bilinear_tap(acc, tv[a + 1][b + 1], vx[a + 1] && vy[b + 1], dx, dy);
                         __stcs(ol + (size_t)(a * D + b) * hw, acc);
                     }
+                }
             }
+            pair_sync(quarter);  // both halves are done reading before the next level
+            w_c += DC_PROF_NOW() - t2;
+        }
+        if (lane == 0 && (warp == 2 || warp == 6)) {
+            DC_PROF_STORE(warp == 2 ? 5 : 10, w_a);
+            DC_PROF_STORE(warp == 2 ? 6 : 11, w_b);
+            DC_PROF_STORE(warp == 2 ? 7 : 12, w_c);
         }
     }
 
@@ -346,6 +465,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
+    if (threadIdx.x == 0) DC_PROF_STORE(0, DC_PROF_NOW() - t_start);
 }
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -368,15 +488,21 @@ EncodeTiledFn get_encode() {
 
 }  // namespace
 
+#ifdef DC_TC_PROFILE
+extern "C" int dc_tc_profile_read(unsigned long long* host, int n) {
+    return (int)cudaMemcpyFromSymbol(host, g_tc_prof, sizeof(unsigned long long) * n);
+}
+#endif
+
 bool dc_tc_supported(const dc_ctx* ctx) {
     const int p = ctx->cfg.precision;
     return (p == DC_PREC_FP16 || p == DC_PREC_BF16) &&
            (ctx->cfg.channels == 64 || ctx->cfg.channels == 128);
 }
 
-// Tensor maps over the store, [max_frames * frame_rows][C] 16-bit elements:
-// A tiles of 128 rows and B chunks of 256 rows, 64 elements (128 bytes) wide,
-// 128-byte swizzle (the canonical K-major operand layout of tcgen05).
+// Tensor map over the store, [max_frames * frame_rows][C] 16-bit elements, with
+// boxes of 128 rows x 64 elements (128 bytes) and 128-byte swizzle: the
+// canonical K-major operand layout of tcgen05, for A tiles and B chunks alike.
 int dc_tc_prepare(dc_ctx* ctx) {
     EncodeTiledFn enc = get_encode();
     if (!enc) return dc_fail(ctx, DC_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
@@ -387,17 +513,13 @@ int dc_tc_prepare(dc_ctx* ctx) {
                           (cuuint64_t)ctx->cfg.max_frames * ctx->frame_rows};
     cuuint64_t strides[1] = {(cuuint64_t)ctx->cfg.channels * 2};
     cuuint32_t estr[2] = {1, 1};
-    cuuint32_t box_a[2] = {64, (cuuint32_t)kTileM};
-    cuuint32_t box_b[2] = {64, (cuuint32_t)kChunkN};
+    static_assert(kTileM == kChunkN, "one box shape serves A tiles and B chunks");
+    cuuint32_t box[2] = {64, (cuuint32_t)kTileM};
     CUresult r1 = enc(reinterpret_cast<CUtensorMap*>(ctx->tmap_a), dt, 2, ctx->store, dims,
-                      strides, box_a, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                       CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    CUresult r2 = enc(reinterpret_cast<CUtensorMap*>(ctx->tmap_b), dt, 2, ctx->store, dims,
-                      strides, box_b, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r1 != CUDA_SUCCESS || r2 != CUDA_SUCCESS)
+    if (r1 != CUDA_SUCCESS)
         return dc_fail(ctx, DC_ERR_CUDA, "cuTensorMapEncodeTiled failed");
     ctx->tc_ready = true;
     return DC_OK;
@@ -420,12 +542,11 @@ int dc_launch_tc(dc_ctx* ctx, const int* ii, const int* jj, int M, const float* 
     const size_t smem = Ly.total + 1024;
     dim3 grid((ctx->hw + kTileM - 1) / kTileM, M);
     const CUtensorMap* ta = reinterpret_cast<const CUtensorMap*>(ctx->tmap_a);
-    const CUtensorMap* tb = reinterpret_cast<const CUtensorMap*>(ctx->tmap_b);
 #define DC_TC_LAUNCH(RR)                                                                   \
     do {                                                                                   \
         auto k = corr_tc_kernel<RR>;                                                       \
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);   \
-        k<<<grid, kThreads, smem, s>>>(*ta, *tb, P);                                       \
+        k<<<grid, kThreads, smem, s>>>(*ta, P);                                       \
     } while (0)
     switch (ctx->cfg.radius) {
         case 0: DC_TC_LAUNCH(0); break;
