@@ -28,10 +28,12 @@ __global__ void __launch_bounds__(256) store_pack_kernel(const Tin* __restrict__
                                                           int first, bool tf32) {
     extern __shared__ float sm[];
     const int C = g.C;
-    float* t0 = sm;             // [C][64]  level 0, tile-local (ty*8+tx)
-    float* t1 = t0 + C * 64;    // [C][16]  level 1
-    float* t2 = t1 + C * 16;    // [C][4]   level 2
-    float* t3 = t2 + C * 4;     // [C][1]   level 3
+    // per-channel rows padded by one float so that the channel-strided reads of
+    // the pixel-major write-out hit distinct banks
+    float* t0 = sm;             // [C][65]  level 0, tile-local (ty*8+tx)
+    float* t1 = t0 + C * 65;    // [C][17]  level 1
+    float* t2 = t1 + C * 17;    // [C][5]   level 2
+    float* t3 = t2 + C * 5;     // [C][1]   level 3
     const int slot_local = blockIdx.z;
     const int slot = first + slot_local;
     const int x0 = blockIdx.x * 8, y0 = blockIdx.y * 8;
@@ -43,7 +45,7 @@ __global__ void __launch_bounds__(256) store_pack_kernel(const Tin* __restrict__
         int y = y0 + (k >> 3), x = x0 + (k & 7);
         float v = 0.0f;
         if (y < g.h && x < g.w) v = dc::to_f32(f[(size_t)c * g.hw + y * g.w + x]);
-        t0[idx] = v;
+        t0[c * 65 + k] = v;
     }
     __syncthreads();
     // level 0 rows
@@ -51,7 +53,7 @@ __global__ void __launch_bounds__(256) store_pack_kernel(const Tin* __restrict__
         int k = idx / C, c = idx % C;
         int y = y0 + (k >> 3), x = x0 + (k & 7);
         if (y < g.h && x < g.w)
-            st[(g.row0[0] + y * g.w + x) * C + c] = pack_value<T>(t0[c * 64 + k], tf32);
+            st[(g.row0[0] + y * g.w + x) * C + c] = pack_value<T>(t0[c * 65 + k], tf32);
     }
     // cascaded pooling inside the tile: level l has (8 >> l)^2 tile-local cells
     float* src = t0;
@@ -62,11 +64,11 @@ __global__ void __launch_bounds__(256) store_pack_kernel(const Tin* __restrict__
         for (int idx = threadIdx.x; idx < C * dw * dw; idx += blockDim.x) {
             int c = idx / (dw * dw), k = idx % (dw * dw);
             int ly = k / dw, lx = k % dw;
-            const float* s = src + c * sw * sw;
+            const float* s = src + c * (sw * sw + (sw > 1));
             float v = s[(2 * ly) * sw + 2 * lx] + s[(2 * ly) * sw + 2 * lx + 1];
             v = v + s[(2 * ly + 1) * sw + 2 * lx];
             v = v + s[(2 * ly + 1) * sw + 2 * lx + 1];
-            dst[idx] = 0.25f * v;
+            dst[c * (dw * dw + (dw > 1)) + k] = 0.25f * v;
         }
         __syncthreads();
         const int gy0 = y0 >> l, gx0 = x0 >> l;
@@ -74,7 +76,7 @@ __global__ void __launch_bounds__(256) store_pack_kernel(const Tin* __restrict__
             int k = idx / C, c = idx % C;
             int y = gy0 + k / dw, x = gx0 + k % dw;
             if (y < g.H[l] && x < g.W[l])
-                st[(g.row0[l] + y * g.W[l] + x) * C + c] = pack_value<T>(dst[c * dw * dw + k], tf32);
+                st[(g.row0[l] + y * g.W[l] + x) * C + c] = pack_value<T>(dst[c * (dw * dw + (dw > 1)) + k], tf32);
         }
         src = dst;
     }
@@ -84,7 +86,7 @@ template <typename Tin, typename T>
 int launch_store_t(dc_ctx* ctx, const void* fmaps, int first, int count, cudaStream_t s) {
     dc::Geom g = dc::geom_of(ctx);
     dim3 grid((g.w + 7) / 8, (g.h + 7) / 8, count);
-    size_t smem = (size_t)g.C * (64 + 16 + 4 + 1) * sizeof(float);
+    size_t smem = (size_t)g.C * (65 + 17 + 5 + 1) * sizeof(float);
     auto k = store_pack_kernel<Tin, T>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     k<<<grid, 256, smem, s>>>((const Tin*)fmaps, (T*)ctx->store, g, first,
