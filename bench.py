@@ -327,9 +327,11 @@ def main():
     if os.path.exists(peaks_path):
         peak, peak_src = float(json.load(open(peaks_path))["hbm_gbs"]), "measured"
     traffic = None
-    tpath = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(tpath):
-        traffic = json.load(open(tpath)).get(f"{wl.name}_{args.precision}")
+    tpath = os.path.join(ROOT, "profiles", f"corr_tc_kernel_{wl.name}.md")
+    if os.path.exists(tpath) and args.precision == "fp16":
+        for ln in open(tpath):
+            if ln.startswith("traffic_bytes_per_launch:"):
+                traffic = int(ln.split(":")[1])
 
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
