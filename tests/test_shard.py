@@ -1,0 +1,63 @@
+"""CPU tests of the multi-GPU host logic: edge partitioning and feature-map
+replication, the latter with world_size-2 gloo process groups."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from slam_hands_b200 import configs
+from slam_hands_b200.shard import edge_range
+
+
+@pytest.mark.parametrize("E,W", [(2048, 8), (2048, 3), (48, 5), (0, 4), (3, 8)])
+def test_edge_ranges_partition(E, W):
+    seen = []
+    for r in range(W):
+        a, b = edge_range(E, W, r)
+        seen.extend(range(a, b))
+        assert b - a in (E // W, E // W + 1)
+    assert seen == list(range(E))
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from slam_hands_b200.shard import replicate_frames
+    wl = configs.WORKLOADS["C2"]
+    fm = torch.from_numpy(configs.make_fmaps_np(wl, frames=3)) if rank == 0 else \
+        torch.zeros(3, wl.channels, wl.h, wl.w)
+    replicate_frames(fm)
+    ii, jj = configs.make_edges(configs.WORKLOADS["C5"])
+    a, b = edge_range(len(ii), world, rank)
+    q.put((rank, float(fm.double().sum()), a, b))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_replication_and_sharding_gloo():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    ref = float(torch.from_numpy(configs.make_fmaps_np(configs.WORKLOADS["C2"], frames=3)).double().sum())
+    assert all(abs(r[1] - ref) < 1e-6 * max(1.0, abs(ref)) for r in res)
+    assert res[0][2] == 0 and res[0][3] == res[1][2] and res[1][3] == 2048
