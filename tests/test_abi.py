@@ -88,3 +88,13 @@ def test_product_path_does_not_reference_the_oracle():
         for f in files:
             if f.endswith((".py", ".cu", ".cuh", ".h", ".cpp")):
                 assert not pat.search(open(os.path.join(root, f)).read()), f
+
+
+def test_cudadroid_shim_header_compiles(tmp_path):
+    # the C++ drop-in for CudaDroid's correlation methods builds against the C ABI
+    src = tmp_path / "shim.cpp"
+    src.write_text('#include "droidcorr_cudadroid.hpp"\nint main() { DroidCorrShim s; return 0; }\n')
+    inc = os.path.dirname(HEADER)
+    r = subprocess.run(["g++", "-std=c++17", "-fsyntax-only", "-I", inc,
+                        "-I", "/usr/local/cuda/include", str(src)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
