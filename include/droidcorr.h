@@ -156,6 +156,27 @@ int dc_alt_lookup(dc_ctx* ctx, const int* ii_dev, const int* jj_dev, int M,
  * DC_ERR_DEVICE_TIMEOUT.  (The reference has no device-side waits.) */
 int dc_device_status(dc_ctx* ctx, dc_stream_t stream);
 
+/* dc_build_and_lookup for callers that may not allocate device memory (no
+ * counterpart in the reference).  Some hosts cannot call cudaMalloc: their
+ * device memory belongs to another allocator or a fixed arena, or allocating
+ * would synchronise the GPU at a bad moment.  This call needs no context: it
+ * packs `num_frames` feature maps (fmaps_dev [num_frames][C][h][w], dtype
+ * DC_DTYPE_*) into a library-owned static device array of 32 MiB and runs the
+ * fused build + pyramid + lookup for M edges into out_dev, allocating nothing.
+ *   - cfg is read as for dc_create (max_frames / max_edges are ignored);
+ *     a packed store larger than 32 MiB is rejected with DC_ERR_INVALID_ARG
+ *     (fp16 at 48x64x128: about 30 frames; at 54x96x128: 19 frames).
+ *   - The array belongs to the current device and is kept until the process
+ *     exits; the first call on each device looks up its address
+ *     (cudaGetSymbolAddress), so make that first call before any stream
+ *     capture.  Each call clears the parts that must start at zero.
+ *   - All calls share the one array: calls that overlap on the GPU (other
+ *     streams, other host threads) race and must be serialised by the caller.
+ *   - Diagnostics go to stderr (there is no context for dc_last_error). */
+int dc_build_and_lookup_static(const dc_config* cfg, const void* fmaps_dev, int dtype,
+                               int num_frames, const int* ii_dev, const int* jj_dev, int M,
+                               const float* coords_dev, float* out_dev, dc_stream_t stream);
+
 /* Number of kernel launches the library has issued on this context (for
  * launch accounting in benchmarks). */
 long long dc_launch_count(const dc_ctx* ctx);

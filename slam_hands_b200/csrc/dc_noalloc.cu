@@ -1,0 +1,129 @@
+// dc_noalloc.cu -- dc_build_and_lookup_static: the fused build + pyramid +
+// lookup for callers that cannot allocate device memory.
+//
+// Some hosts of this library may not call cudaMalloc at all: a process whose
+// device memory is owned by another allocator (a caching pool that must see
+// every allocation, a fixed pre-partitioned arena on a shared GPU), or code that
+// runs where allocating would synchronise the device or fail for lack of
+// memory at an unpredictable moment.  For them this entry point takes no
+// context: the packed keyframe store that dc_build_and_lookup keeps in its
+// context lives here in one file-scope device array of fixed size, shared by
+// all calls in the process on a given GPU.
+#include <cstdio>
+
+#include "dc_internal.cuh"
+
+namespace {
+
+// 32 MiB: room for 16 keyframes of a 54x96x128 fp16 pyramid (1.76 MB each),
+// or 30 of 48x64x128.  Every GPU that loads the library holds it until exit.
+constexpr size_t kScratchBytes = size_t(32) << 20;
+constexpr int kMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_scratch[kScratchBytes];
+static __device__ int g_scratch_err;
+
+// Device addresses of the arrays, looked up once per device (host code may not
+// use the symbols themselves: on the host they are stand-ins, not addresses).
+struct DeviceScratch {
+    bool ready = false;
+    void* store = nullptr;
+    int* err = nullptr;
+};
+DeviceScratch g_dev[kMaxDevices];
+
+int scratch_for_device(int dev, DeviceScratch** out) {
+    if (dev < 0 || dev >= kMaxDevices) return DC_ERR_UNSUPPORTED;
+    DeviceScratch& d = g_dev[dev];
+    if (!d.ready) {
+        if (cudaGetSymbolAddress(&d.store, g_scratch) != cudaSuccess ||
+            cudaGetSymbolAddress(reinterpret_cast<void**>(&d.err), g_scratch_err) !=
+                cudaSuccess) {
+            cudaGetLastError();
+            return DC_ERR_CUDA;
+        }
+        d.ready = true;
+    }
+    *out = &d;
+    return DC_OK;
+}
+
+// Diagnostics go to stderr: this entry point has no context to keep a message.
+int fail(int status, const char* msg) {
+    std::fprintf(stderr, "dc_build_and_lookup_static: %s\n", msg);
+    return status;
+}
+
+}  // namespace
+
+extern "C" {
+
+int dc_build_and_lookup_static(const dc_config* cfg, const void* fmaps, int dtype,
+                               int num_frames, const int* ii, const int* jj, int M,
+                               const float* coords, float* out, dc_stream_t stream) {
+    if (!cfg) return fail(DC_ERR_INVALID_ARG, "cfg is NULL");
+    const dc_config& c = *cfg;
+    if (c.h < 1 || c.w < 1 || (long long)c.h * c.w > DC_MAX_HW ||
+        (c.channels != 32 && c.channels != 64 && c.channels != 128 && c.channels != 256) ||
+        c.levels < 1 || c.levels > DC_MAX_LEVELS || c.radius < 0 || c.radius > DC_MAX_RADIUS ||
+        c.precision < DC_PREC_FP32 || c.precision > DC_PREC_FP16 ||
+        (c.h >> (c.levels - 1)) < 1 || (c.w >> (c.levels - 1)) < 1)
+        return fail(DC_ERR_INVALID_ARG, "invalid dc_config");
+    if (dtype != DC_DTYPE_F32 && dtype != DC_DTYPE_F16)
+        return fail(DC_ERR_INVALID_ARG, "dtype must be DC_DTYPE_F32 or DC_DTYPE_F16");
+    if (num_frames < 1 || M < 0) return fail(DC_ERR_INVALID_ARG, "num_frames < 1 or M < 0");
+    if (M == 0) return DC_OK;
+    if (!fmaps || !ii || !jj || !coords || !out) return fail(DC_ERR_INVALID_ARG, "NULL pointer");
+
+    // the context a dc_create would build, on the stack, over the static store
+    dc_ctx ctx;
+    ctx.cfg = c;
+    ctx.cfg.max_frames = num_frames;
+    ctx.cfg.max_edges = M;
+    ctx.hw = c.h * c.w;
+    long long rows = 0;
+    for (int l = 0; l < DC_MAX_LEVELS; l++) {
+        ctx.H[l] = c.h >> l;
+        ctx.W[l] = c.w >> l;
+        ctx.level_row0[l] = rows;
+        if (l < c.levels)
+            rows += ((long long)ctx.H[l] * ctx.W[l] + DC_ROW_PAD - 1) / DC_ROW_PAD * DC_ROW_PAD;
+    }
+    ctx.frame_rows = rows;
+    ctx.elem_bytes = (c.precision == DC_PREC_FP16 || c.precision == DC_PREC_BF16) ? 2 : 4;
+    ctx.store_bytes = (long long)num_frames * rows * c.channels * ctx.elem_bytes;
+    if (ctx.store_bytes > (long long)kScratchBytes) {
+        char msg[200];
+        std::snprintf(msg, sizeof msg,
+                      "%d frames need %lld bytes of packed store; the static scratch holds %lld",
+                      num_frames, ctx.store_bytes, (long long)kScratchBytes);
+        return fail(DC_ERR_INVALID_ARG, msg);
+    }
+    if (cudaGetDevice(&ctx.device) != cudaSuccess) return fail(DC_ERR_CUDA, "cudaGetDevice failed");
+    cudaDeviceGetAttribute(&ctx.num_sms, cudaDevAttrMultiProcessorCount, ctx.device);
+    DeviceScratch* ds = nullptr;
+    int rc = scratch_for_device(ctx.device, &ds);
+    if (rc) return fail(rc, "cudaGetSymbolAddress of the static scratch failed");
+    ctx.store = ds->store;
+    ctx.dev_err = ds->err;
+
+    cudaStream_t s = (cudaStream_t)stream;
+    // the store's padding rows and the error word must start at zero; the
+    // previous call left its contents behind
+    if (cudaMemsetAsync(ctx.store, 0, (size_t)ctx.store_bytes, s) != cudaSuccess ||
+        cudaMemsetAsync(ctx.dev_err, 0, sizeof(int), s) != cudaSuccess)
+        return fail(DC_ERR_CUDA, "clearing the static scratch failed");
+    rc = dc_launch_store(&ctx, fmaps, dtype, 0, num_frames, s);
+    if (rc) return fail(rc, ctx.err.c_str());
+    if (dc_tc_supported(&ctx)) {
+        rc = dc_tc_prepare(&ctx);
+        if (rc) return fail(rc, ctx.err.c_str());
+        rc = dc_launch_tc(&ctx, ii, jj, M, coords, out, s);
+    } else {
+        rc = dc_launch_alt(&ctx, ii, jj, M, coords, out, s);
+    }
+    if (rc) return fail(rc, ctx.err.c_str());
+    return DC_OK;
+}
+
+}  // extern "C"
