@@ -40,14 +40,16 @@ using namespace dc::sm100;
 
 constexpr int kTileM = 128;      // source pixels per CTA = MMA M = TMEM lanes
 constexpr int kChunkN = 128;     // max target pixels per chunk = MMA N
-constexpr int kHalfCols = 64;    // chunk columns per epilogue warp
-constexpr int kStagesB = 2;      // shared-memory stages of target rows
+constexpr int kSubCols = 32;     // chunk columns per epilogue warp
+constexpr int kStagesB = 3;      // shared-memory stages of target rows
 constexpr int kAcc = 4;          // TMEM accumulators (kAcc * kChunkN = 512 columns)
-constexpr int kEpiWarps = 8;     // two warps per TMEM lane quarter
+constexpr int kSubWarps = 4;     // epilogue warps per TMEM lane quarter
+constexpr int kPasses = kChunkN / (kSubWarps * 32);  // 32-column passes per warp and chunk
+constexpr int kEpiWarps = 4 * kSubWarps;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kMaxChunks = 256;
 constexpr int kWinStride = 65;   // floats per pixel window row (64 taps + pad)
-constexpr int kStStride = kHalfCols + 4;  // floats per staged TMEM row (16-byte rows)
+constexpr int kStStride = 12;   // floats per staging row: 3 16-byte groups (bank-conflict free)
 constexpr uint32_t kTmemCols = kAcc * kChunkN;
 constexpr uint32_t kRowBytes = 128;  // one 128-byte K atom per operand row
 
@@ -56,7 +58,8 @@ constexpr uint32_t kRowBytes = 128;  // one 128-byte K atom per operand row
 struct ChunkDesc {
     int level, n, row;     // MMA N (multiple of 16), store row of the first pixel
     int y0, x0, seg;       // level coordinates of chunk column 0, segment length
-    int rlo[2], rhi[2];    // chunk rows touched by columns [64h, 64h + 64), h = 0, 1
+    int cols;              // valid columns (nrows * seg)
+    int rlo[4], rhi[4];    // chunk rows touched by 32-column pass q (rhi < 0: none)
 };
 
 struct TcParams {
@@ -120,15 +123,15 @@ __device__ unsigned long long g_tc_prof[8192 * 16];
     } while (0)
 #endif
 
-__device__ __forceinline__ void pair_sync(int quarter) {
-    asm volatile("bar.sync %0, %1;" ::"r"(1 + quarter), "r"(64) : "memory");
+// Named barrier of the kSubWarps epilogue warps that share a TMEM lane quarter.
+__device__ __forceinline__ void quarter_sync(int quarter) {
+    asm volatile("bar.sync %0, %1;" ::"r"(1 + quarter), "r"(32 * kSubWarps) : "memory");
 }
 
 template <int R>
 __global__ void __launch_bounds__(kThreads, 1)
     corr_tc_kernel(const __grid_constant__ CUtensorMap tmap, TcParams P) {
     constexpr int D = 2 * R + 1, NW = 2 * R + 2;
-    constexpr int ASPLIT = (D + 1) / 2;  // epilogue half 0 forms outputs a < ASPLIT
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -163,7 +166,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const bool epi = warp >= 2;
     const int quarter = warp & 3;            // TMEM lane quarter of this warp
-    const int half = (warp - 2) >> 2;        // 0: warps 2-5, 1: warps 6-9
+    const int sub = (warp - 2) >> 2;         // which 32-column slice of a chunk (0..3)
     const int ti = 32 * quarter + lane;      // tile pixel (epilogue threads)
     const int p = p0 + ti;
     const bool pv = epi && p < hw;
@@ -209,49 +212,67 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 
     // ---- 1. target-row range per level over this tile's windows
-    if (pv && half == 0) {
+    if (epi && sub == 0) {
         for (int l = 0; l < g.levels; l++) {
             const float sc = 1.0f / (float)(1 << l);
             const int by = (int)floorf(cy * sc) - R, bx = (int)floorf(cx * sc) - R;
-            const int lo = max(by, 0), hi = min(by + NW - 1, g.H[l] - 1);
+            int lo = max(by, 0), hi = min(by + NW - 1, g.H[l] - 1);
             const bool xin = bx + NW - 1 >= 0 && bx < g.W[l];
-            if (lo <= hi && xin) {
+            if (!(pv && lo <= hi && xin)) {
+                lo = 0x7fffffff;
+                hi = -1;
+            }
+            lo = __reduce_min_sync(0xffffffffu, lo);
+            hi = __reduce_max_sync(0xffffffffu, hi);
+            if (lane == 0 && lo <= hi) {
                 atomicMin(&misc[kMiscRange + 2 * l], lo);
                 atomicMax(&misc[kMiscRange + 2 * l + 1], hi);
             }
         }
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        int n = 0;
-        for (int l = 0; l < g.levels; l++) {
-            const int ylo = misc[kMiscRange + 2 * l], yhi = misc[kMiscRange + 2 * l + 1];
-            if (ylo > yhi) continue;
-            const int Wl = g.W[l];
-            const int rows_per = Wl <= kChunkN ? kChunkN / Wl : 1;
-            const int seg_max = Wl <= kChunkN ? Wl : kChunkN;
-            for (int y = ylo; y <= yhi; y += rows_per) {
-                const int nrows = min(rows_per, yhi - y + 1);
-                for (int x = 0; x < Wl && n < kMaxChunks; x += seg_max) {
-                    ChunkDesc c;
-                    c.level = l;
-                    c.y0 = y;
-                    c.x0 = x;
-                    c.seg = min(seg_max, Wl - x);
-                    const int cols = nrows * c.seg;
-                    c.n = (cols + 15) & ~15;
-                    c.row = (int)((long long)sj * g.frame_rows + g.row0[l] + y * Wl + x);
-                    for (int h = 0; h < 2; h++) {
-                        c.rlo[h] = (h * kHalfCols) / c.seg;
-                        c.rhi[h] = min(cols - 1, h * kHalfCols + kHalfCols - 1) / c.seg;
-                        if (h * kHalfCols >= cols) c.rhi[h] = -1;
-                    }
-                    chunks[n++] = c;
-                }
-            }
-        }
-        misc[kMiscCount] = n;
+    // chunk schedule: every thread derives the per-level counts (a few integer
+    // ops), then thread t fills descriptor t, so no thread builds the list alone
+    int lvl_first[DC_MAX_LEVELS + 1], nchunks_all = 0;
+    for (int l = 0; l < DC_MAX_LEVELS; l++) {
+        lvl_first[l] = nchunks_all;
+        const int ylo = misc[kMiscRange + 2 * l], yhi = misc[kMiscRange + 2 * l + 1];
+        if (l >= g.levels || ylo > yhi) continue;
+        const int Wl = g.W[l];
+        const int rows_per = Wl <= kChunkN ? kChunkN / Wl : 1;
+        const int segs = Wl <= kChunkN ? 1 : (Wl + kChunkN - 1) / kChunkN;
+        nchunks_all += (yhi - ylo + rows_per) / rows_per * segs;
     }
+    lvl_first[DC_MAX_LEVELS] = nchunks_all;
+    nchunks_all = min(nchunks_all, kMaxChunks);
+    for (int t = threadIdx.x; t < nchunks_all; t += kThreads) {
+        int l = 0;
+        while (t >= lvl_first[l + 1]) l++;
+        const int ylo = misc[kMiscRange + 2 * l], yhi = misc[kMiscRange + 2 * l + 1];
+        const int Wl = g.W[l];
+        const int rows_per = Wl <= kChunkN ? kChunkN / Wl : 1;
+        const int seg_max = Wl <= kChunkN ? Wl : kChunkN;
+        const int segs = (Wl + seg_max - 1) / seg_max;
+        const int idx = t - lvl_first[l];
+        const int r = segs > 1 ? idx / segs : idx, sg = segs > 1 ? idx - r * segs : 0;
+        ChunkDesc c;
+        c.level = l;
+        c.y0 = ylo + r * rows_per;
+        c.x0 = sg * seg_max;
+        c.seg = min(seg_max, Wl - c.x0);
+        const int nrows = min(rows_per, yhi - c.y0 + 1);
+        const int cols = nrows * c.seg;
+        c.n = (cols + 15) & ~15;
+        c.row = (int)((long long)sj * g.frame_rows + g.row0[l] + c.y0 * Wl + c.x0);
+        c.cols = cols;
+        for (int q = 0; q < 4; q++) {
+            const int cb = 32 * q;
+            c.rlo[q] = cb / c.seg;
+            c.rhi[q] = cb < cols ? min(cols - 1, cb + 31) / c.seg : -1;
+        }
+        chunks[t] = c;
+    }
+    if (threadIdx.x == 0) misc[kMiscCount] = nchunks_all;
     __syncthreads();
     const int nchunks = misc[kMiscCount];
     if (threadIdx.x == 0) {
@@ -320,7 +341,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const uint64_t ad = sdesc_sw128(sA + at * kTileM * kRowBytes + wi * 32);
                         const uint64_t bd =
                             sdesc_sw128(sB + s * Ly.stage_b + at * kChunkN * kRowBytes + wi * 32);
+#if !(defined(DC_TC_EXP) && DC_TC_EXP == 4)
                         mma_f16(d, ad, bd, idesc, kk > 0 ? 1u : 0u);
+#endif
                     }
                     mma_commit(bar(kBarEmpty + s));
                     mma_commit(bar(kBarTFull + a));
@@ -336,7 +359,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         float* win = win_base + ti * kWinStride;
         float* st = st_base + ((warp - 2) * 32 + lane) * kStStride;
         const uint32_t tl = tmem + ((uint32_t)(32 * quarter) << 16);
-        const int cbase = kHalfCols * half;
+        const int cwarp = kSubCols * kPasses * sub;  // first chunk column of this warp
         int c = 0;
         bool alive = true;
         for (int l = 0; l < g.levels && alive; l++) {
@@ -354,57 +377,70 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t par = (c / kAcc) & 1;
                 const long long t0 = DC_PROF_NOW();
                 int okw = 1;
+#if defined(DC_TC_EXP) && DC_TC_EXP == 3
+                (void)par;
+#else
                 if (lane == 0) okw = mbar_wait(bar(kBarTFull + a), par, abort) ? 1 : 0;
+#endif
                 okw = __shfl_sync(0xffffffffu, okw, 0);
                 if (!okw) {
                     if (lane == 0) raise_abort(abort, P.err, 5);
                     alive = false;
                     break;
                 }
+#if !(defined(DC_TC_EXP) && DC_TC_EXP == 3)
                 mbar_wait(bar(kBarTFull + a), par, abort);
+#endif
                 tc_fence_after();
                 const long long t1 = DC_PROF_NOW();
                 w_a += t1 - t0;
                 const ChunkDesc& ch = chunks[c];
-                const int rlo = half ? ch.rlo[1] : ch.rlo[0];
-                const int rhi = half ? ch.rhi[1] : ch.rhi[0];
-                if (rhi >= 0) {
-                    // window rows of this pixel inside this warp's chunk rows
-                    const int ya = max(ylo, ch.y0 + rlo);
-                    const int yb = min(yhi, ch.y0 + rhi);
-                    // this pixel's taps in staged-column coordinates: row y, tap x
-                    // sits at column (y - y0) * seg + (x - x0) - cbase
-                    const int xa = max(xlo, ch.x0), xb = min(xhi, ch.x0 + ch.seg - 1);
-                    const bool need = any && ya <= yb && xa <= xb;
-                    if (__any_sync(0xffffffffu, need)) {
-                        float v[kHalfCols];
-                        tmem_ld64(tl + (uint32_t)(a * kChunkN + cbase), v);
-                        if (need) {
-                            const int kofs = -ch.x0 - cbase;
-                            const int klo = max((ya - ch.y0) * ch.seg + xa + kofs, 0);
-                            const int khi = min((yb - ch.y0) * ch.seg + xb + kofs, kHalfCols - 1);
-                            // stage only the 16-byte groups spanning this pixel's taps
-                            float4* st4 = reinterpret_cast<float4*>(st);
 #pragma unroll
-                            for (int k = 0; k < kHalfCols / 4; k++)
-                                if (4 * k + 3 >= klo && 4 * k <= khi)
-                                    st4[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2],
-                                                         v[4 * k + 3]);
-                            for (int y = ya; y <= yb; y++) {
-                                const int k0 = (y - ch.y0) * ch.seg + bx + kofs;
-                                float tv[NW];
+                for (int pass = 0; pass < kPasses; pass++) {
+                const int cb = cwarp + kSubCols * pass;
+                    const int qi = cb / kSubCols;
+                    if (ch.rhi[qi] >= 0) {
+                        const int rlo = ch.rlo[qi];
+                        const int rhi = ch.rhi[qi];
+                        // window rows of this pixel inside this warp's chunk rows
+                        const int ya = max(ylo, ch.y0 + rlo);
+                        const int yb = min(yhi, ch.y0 + rhi);
+                        // this pixel's taps in staged-column coordinates: row y, tap x
+                        // sits at column (y - y0) * seg + (x - x0) - cb
+                        const int xa = max(xlo, ch.x0), xb = min(xhi, ch.x0 + ch.seg - 1);
+                        const bool need = any && ya <= yb && xa <= xb;
+                        if (__any_sync(0xffffffffu, need)) {
+                            float v[kSubCols];
+                            tmem_ld32(tl + (uint32_t)(a * kChunkN + cb), v);
+                            if (need) {
+                                const int kofs = -ch.x0 - cb;
+                                // valid taps i of a row: x = bx + i in [xa, xb] and staged
+                                // column k0 + i in [0, 32); branch-free predicates
+                                const int ia = xa - bx, ib = xb - bx;
+                                for (int y = ya; y <= yb; y++) {
+                                    const int k0 = (y - ch.y0) * ch.seg + bx + kofs;
+                                    const int lo = max(ia, -k0), hi = min(ib, kSubCols - 1 - k0);
+                                    if (lo > hi) continue;
+                                    const unsigned span = (unsigned)(hi - lo);
+                                    // stage the <= 3 16-byte groups holding this row's taps,
+                                    // compacted: group g goes to slot g - g0
+                                    const int g0 = (k0 + lo) >> 2;
+                                    const unsigned gspan = (unsigned)(((k0 + hi) >> 2) - g0);
+                                    float4* st4 = reinterpret_cast<float4*>(st);
 #pragma unroll
-                                for (int i = 0; i < NW; i++) {
-                                    const int x = bx + i, k = k0 + i;
-                                    tv[i] = (x >= xa && x <= xb && k >= 0 && k < kHalfCols)
-                                                ? st[k] : 0.0f;
-                                }
-                                float* wcol = win + (y - by);
+                                    for (int k = 0; k < kSubCols / 4; k++)
+                                        if ((unsigned)(k - g0) <= gspan)
+                                            st4[k - g0] = make_float4(v[4 * k], v[4 * k + 1],
+                                                                      v[4 * k + 2], v[4 * k + 3]);
+                                    const float* sk = st + (k0 - 4 * g0);
+                                    float tv[NW];
 #pragma unroll
-                                for (int i = 0; i < NW; i++) {
-                                    const int x = bx + i, k = k0 + i;
-                                    if (x >= xa && x <= xb && k >= 0 && k < kHalfCols)
-                                        wcol[i * 8] = g.alpha * tv[i];
+                                    for (int i = 0; i < NW; i++)
+                                        tv[i] = ((unsigned)(i - lo) <= span) ? sk[i] : 0.0f;
+                                    float* wcol = win + (y - by);
+#pragma unroll
+                                    for (int i = 0; i < NW; i++)
+                                        if ((unsigned)(i - lo) <= span) wcol[i * 8] = g.alpha * tv[i];
                                 }
                             }
                         }
@@ -418,38 +454,43 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (!alive) break;
             const long long t2 = DC_PROF_NOW();
-            pair_sync(quarter);  // both halves have written this level's windows
+            quarter_sync(quarter);  // all slices have written this level's windows
             if (pv) {
-                bool vx[NW], vy[NW];
+                bool vy[NW];
 #pragma unroll
-                for (int k = 0; k < NW; k++) {
-                    vx[k] = (unsigned)(bx + k) < (unsigned)Wl;
-                    vy[k] = (unsigned)(by + k) < (unsigned)Hl;
-                }
+                for (int k = 0; k < NW; k++) vy[k] = (unsigned)(by + k) < (unsigned)Hl;
                 const float ux = 1.0f - dx, uy = 1.0f - dy;
                 float* ol = out_e + (size_t)(l * D * D) * hw + p;
-                const int a0 = half ? ASPLIT : 0, a1 = half ? D : ASPLIT;
-                float tv[NW][NW];
+                // the quarter's warps split the output columns a: 2, 2, 2, 1 (R = 3)
+                constexpr int AW = (D + kSubWarps - 1) / kSubWarps;  // columns per warp
+                const int a0 = sub * AW;
+                // taps of columns a0 .. a0 + AW (registers indexed statically)
+                float tv[AW + 1][NW];
+                bool vxa[AW + 1];
 #pragma unroll
-                for (int i = 0; i < NW; i++)
+                for (int ii = 0; ii <= AW; ii++) {
+                    const int i = a0 + ii;
+                    vxa[ii] = i < NW && (unsigned)(bx + i) < (unsigned)Wl;
 #pragma unroll
                     for (int j = 0; j < NW; j++)
-                        tv[i][j] = (i >= a0 && i <= a1 && vx[i] && vy[j]) ? win[i * 8 + j] : 0.0f;
+                        tv[ii][j] = (vxa[ii] && vy[j]) ? win[i * 8 + j] : 0.0f;
+                }
 #pragma unroll
-                for (int a = 0; a < D; a++) {
-                    if (a < a0 || a >= a1) continue;
+                for (int ai = 0; ai < AW; ai++) {
+                    const int a = a0 + ai;
+                    if (a >= D) break;
 #pragma unroll
                     for (int b = 0; b < D; b++) {
                         float acc = 0.0f;
-                        acc = dc::bilinear_tap(acc, tv[a][b], vx[a] && vy[b], ux, uy);
-                        acc = dc::bilinear_tap(acc, tv[a][b + 1], vx[a] && vy[b + 1], ux, dy);
-                        acc = dc::bilinear_tap(acc, tv[a + 1][b], vx[a + 1] && vy[b], dx, uy);
-                        acc = dc::bilinear_tap(acc, tv[a + 1][b + 1], vx[a + 1] && vy[b + 1], dx, dy);
+                        acc = dc::bilinear_tap(acc, tv[ai][b], vxa[ai] && vy[b], ux, uy);
+                        acc = dc::bilinear_tap(acc, tv[ai][b + 1], vxa[ai] && vy[b + 1], ux, dy);
+                        acc = dc::bilinear_tap(acc, tv[ai + 1][b], vxa[ai + 1] && vy[b], dx, uy);
+                        acc = dc::bilinear_tap(acc, tv[ai + 1][b + 1], vxa[ai + 1] && vy[b + 1], dx, dy);
                         __stcs(ol + (size_t)(a * D + b) * hw, acc);
                     }
                 }
             }
-            pair_sync(quarter);  // both halves are done reading before the next level
+            quarter_sync(quarter);  // all are done reading before the next level
             w_c += DC_PROF_NOW() - t2;
         }
         if (lane == 0 && (warp == 2 || warp == 6)) {
