@@ -144,19 +144,21 @@ def run_reference_arm(args, wl):
     from oracle import oracle as O
 
     O.lib()
+    # all host threads (torchrun sets OMP_NUM_THREADS=1 for its workers)
+    threads = len(os.sched_getaffinity(0))
     per_step = 2  # edges per step: a bounded sample of the batch
     times = []
     for s in range(args.warmup + args.steps):
         e0 = (s * per_step) % len(ii)
         sl = slice(e0, e0 + per_step)
         t0 = time.perf_counter()
-        O.cpu_build_and_sample(fm_np, ii[sl], jj[sl], coords[sl], wl.alpha)
+        O.cpu_build_and_sample(fm_np, ii[sl], jj[sl], coords[sl], wl.alpha, threads=threads)
         dt = time.perf_counter() - t0
         if s >= args.warmup:
             times.append(dt)
     tot = sum(times)
     value = per_step * len(times) / tot
-    cores = O.max_threads()
+    cores = threads
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * tot / len(times), "higher_is_better": True,
@@ -380,7 +382,8 @@ def main():
 
     if not args.no_cpu_baseline and world == 1:
         fm_np = fm.cpu().numpy()
-        v, n, cores = cpu_sample(wl, fm_np, np.asarray(ii), np.asarray(jj), coords.cpu().numpy())
+        v, n, cores = cpu_sample(wl, fm_np, np.asarray(ii), np.asarray(jj), coords.cpu().numpy(),
+                                 threads=len(os.sched_getaffinity(0)))
         line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
                                 "sample": f"{n} edges of {wl.name} (fp32 C/OpenMP oracle)"}
     print(json.dumps(line), flush=True)
