@@ -39,15 +39,14 @@ namespace {
 using namespace dc::sm100;
 
 constexpr int kTileM = 128;      // source pixels per CTA = MMA M = TMEM lanes
-constexpr int kChunkN = 128;     // max target pixels per chunk = MMA N
+constexpr int kChunkN = 256;     // max target pixels per chunk = MMA N
 constexpr int kSubCols = 32;     // chunk columns per epilogue warp
-constexpr int kStagesB = 3;      // shared-memory stages of target rows
-constexpr int kAcc = 4;          // TMEM accumulators (kAcc * kChunkN = 512 columns)
+constexpr int kStagesB = 2;      // shared-memory stages of target rows
+constexpr int kAcc = 2;          // TMEM accumulators (kAcc * kChunkN = 512 columns)
 constexpr int kSubWarps = 4;     // epilogue warps per TMEM lane quarter
 constexpr int kPasses = kChunkN / (kSubWarps * 32);  // 32-column passes per warp and chunk
 constexpr int kEpiWarps = 4 * kSubWarps;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
-constexpr int kMaxChunks = 256;
 constexpr int kWinStride = 65;   // floats per pixel window row (64 taps + pad)
 constexpr int kStStride = 12;   // floats per staging row: 3 16-byte groups (bank-conflict free)
 constexpr uint32_t kTmemCols = kAcc * kChunkN;
@@ -56,11 +55,40 @@ constexpr uint32_t kRowBytes = 128;  // one 128-byte K atom per operand row
 // A chunk is `nrows` consecutive target rows of one level, each the segment
 // [x0, x0 + seg) of the row (seg = W when whole rows fit, else a row is split).
 struct ChunkDesc {
-    int level, n, row;     // MMA N (multiple of 16), store row of the first pixel
-    int y0, x0, seg;       // level coordinates of chunk column 0, segment length
-    int cols;              // valid columns (nrows * seg)
-    int rlo[4], rhi[4];    // chunk rows touched by 32-column pass q (rhi < 0: none)
+    int n, row;            // MMA N (multiple of 16), store row of the first pixel
+    int y0, x0, seg, cols; // level coordinates of chunk column 0, segment, columns
 };
+
+// Per-level chunk schedule of one tile: chunks first .. first+count-1 cover the
+// target rows ylo..yhi of the level, rows_per whole rows per chunk, or for rows
+// wider than a chunk, segs segments of seg_max pixels per row.
+struct LevelSched {
+    int first, count, ylo, yhi, rows_per, seg_max, segs, W;
+};
+
+__device__ __forceinline__ ChunkDesc make_chunk(const LevelSched& L, int idx,
+                                                long long row_base) {
+    ChunkDesc c;
+    int r = idx, sg = 0;
+    if (L.segs > 1) {
+        r = idx / L.segs;
+        sg = idx - r * L.segs;
+    }
+    c.y0 = L.ylo + r * L.rows_per;
+    c.x0 = sg * L.seg_max;
+    c.seg = min(L.seg_max, L.W - c.x0);
+    c.cols = min(L.rows_per, L.yhi - c.y0 + 1) * c.seg;
+    c.n = (c.cols + 15) & ~15;
+    c.row = (int)(row_base + (long long)c.y0 * L.W + c.x0);
+    return c;
+}
+
+// floor(v / d) for 0 <= v < 2^12 and 1 <= d <= 2^12 from d's reciprocal: the
+// quotient of v + 0.5 is at least 0.5 / d away from an integer, far above the
+// rounding error of the product.
+__device__ __forceinline__ int div_small(int v, float inv_d) {
+    return (int)(((float)v + 0.5f) * inv_d);
+}
 
 struct TcParams {
     dc::Geom g;
@@ -86,8 +114,8 @@ __host__ __device__ constexpr Layout make_layout(int atoms) {
     L.win = L.b + kStagesB * L.stage_b;
     L.st = L.win + kTileM * kWinStride * 4;
     L.chunks = L.st + kEpiWarps * 32 * kStStride * 4;
-    L.bars = L.chunks + kMaxChunks * sizeof(ChunkDesc);
-    L.misc = L.bars + 16 * 8;
+    L.bars = L.chunks + DC_MAX_LEVELS * sizeof(LevelSched);
+    L.misc = L.bars + 24 * 8;
     L.total = L.misc + 64;
     return L;
 }
@@ -98,7 +126,7 @@ enum { kMiscTmem = 0, kMiscAbort = 1, kMiscCount = 2, kMiscRange = 4 };  // rang
 // barrier slots
 enum { kBarA = 0, kBarFull = 1, kBarEmpty = kBarFull + kStagesB,
        kBarTFull = kBarEmpty + kStagesB, kBarTEmpty = kBarTFull + kAcc };
-static_assert(kBarTEmpty + kAcc <= 16, "barrier slots");
+static_assert(kBarTEmpty + kAcc <= 24, "barrier slots");
 
 __device__ __forceinline__ void raise_abort(volatile int* abort, int* err, int code) {
     *abort = 1;
@@ -158,7 +186,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t sB = smem_addr(base + Ly.b);
     float* win_base = reinterpret_cast<float*>(base + Ly.win);
     float* st_base = reinterpret_cast<float*>(base + Ly.st);
-    ChunkDesc* chunks = reinterpret_cast<ChunkDesc*>(base + Ly.chunks);
+    LevelSched* sched = reinterpret_cast<LevelSched*>(base + Ly.chunks);
     const uint32_t bars = smem_addr(base + Ly.bars);
     int* misc = reinterpret_cast<int*>(base + Ly.misc);
     volatile int* abort = misc + kMiscAbort;
@@ -231,48 +259,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
     __syncthreads();
-    // chunk schedule: every thread derives the per-level counts (a few integer
-    // ops), then thread t fills descriptor t, so no thread builds the list alone
-    int lvl_first[DC_MAX_LEVELS + 1], nchunks_all = 0;
-    for (int l = 0; l < DC_MAX_LEVELS; l++) {
-        lvl_first[l] = nchunks_all;
-        const int ylo = misc[kMiscRange + 2 * l], yhi = misc[kMiscRange + 2 * l + 1];
-        if (l >= g.levels || ylo > yhi) continue;
-        const int Wl = g.W[l];
-        const int rows_per = Wl <= kChunkN ? kChunkN / Wl : 1;
-        const int segs = Wl <= kChunkN ? 1 : (Wl + kChunkN - 1) / kChunkN;
-        nchunks_all += (yhi - ylo + rows_per) / rows_per * segs;
-    }
-    lvl_first[DC_MAX_LEVELS] = nchunks_all;
-    nchunks_all = min(nchunks_all, kMaxChunks);
-    for (int t = threadIdx.x; t < nchunks_all; t += kThreads) {
-        int l = 0;
-        while (t >= lvl_first[l + 1]) l++;
-        const int ylo = misc[kMiscRange + 2 * l], yhi = misc[kMiscRange + 2 * l + 1];
-        const int Wl = g.W[l];
-        const int rows_per = Wl <= kChunkN ? kChunkN / Wl : 1;
-        const int seg_max = Wl <= kChunkN ? Wl : kChunkN;
-        const int segs = (Wl + seg_max - 1) / seg_max;
-        const int idx = t - lvl_first[l];
-        const int r = segs > 1 ? idx / segs : idx, sg = segs > 1 ? idx - r * segs : 0;
-        ChunkDesc c;
-        c.level = l;
-        c.y0 = ylo + r * rows_per;
-        c.x0 = sg * seg_max;
-        c.seg = min(seg_max, Wl - c.x0);
-        const int nrows = min(rows_per, yhi - c.y0 + 1);
-        const int cols = nrows * c.seg;
-        c.n = (cols + 15) & ~15;
-        c.row = (int)((long long)sj * g.frame_rows + g.row0[l] + c.y0 * Wl + c.x0);
-        c.cols = cols;
-        for (int q = 0; q < 4; q++) {
-            const int cb = 32 * q;
-            c.rlo[q] = cb / c.seg;
-            c.rhi[q] = cb < cols ? min(cols - 1, cb + 31) / c.seg : -1;
+    if (threadIdx.x == 0) {
+        int n = 0;
+        for (int l = 0; l < DC_MAX_LEVELS; l++) {
+            LevelSched L;
+            L.first = n;
+            L.count = 0;
+            L.ylo = misc[kMiscRange + 2 * l];
+            L.yhi = misc[kMiscRange + 2 * l + 1];
+            L.W = max(g.W[l], 1);
+            L.rows_per = L.W <= kChunkN ? kChunkN / L.W : 1;
+            L.seg_max = L.W <= kChunkN ? L.W : kChunkN;
+            L.segs = (L.W + L.seg_max - 1) / L.seg_max;
+            if (l < g.levels && L.ylo <= L.yhi)
+                L.count = (L.yhi - L.ylo + L.rows_per) / L.rows_per * L.segs;
+            n += L.count;
+            sched[l] = L;
         }
-        chunks[t] = c;
+        misc[kMiscCount] = n;
     }
-    if (threadIdx.x == 0) misc[kMiscCount] = nchunks_all;
     __syncthreads();
     const int nchunks = misc[kMiscCount];
     if (threadIdx.x == 0) {
@@ -286,7 +291,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             const uint32_t b_bytes = Ly.stage_b;
             int issued = 0;
+            int lv = 0;
             for (int c = 0; c < nchunks; c++) {
+                while (c >= sched[lv].first + sched[lv].count) lv++;
                 const int s = c % kStagesB;
                 const long long t0 = DC_PROF_NOW();
                 if (c >= kStagesB &&
@@ -296,10 +303,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 w_a += DC_PROF_NOW() - t0;
                 mbar_arrive_expect_tx(bar(kBarFull + s), b_bytes);
-                const int row = chunks[c].row;
+                const int row = make_chunk(sched[lv], c - sched[lv].first,
+                                           (long long)sj * g.frame_rows + g.row0[lv]).row;
                 for (int k = 0; k < P.atoms; k++)
-                    tma_load_2d(sB + s * Ly.stage_b + k * kChunkN * kRowBytes, &tmap, k * 64, row,
-                                bar(kBarFull + s));
+                    for (int h = 0; h < kChunkN / kTileM; h++)  // boxes of 128 rows
+                        tma_load_2d(sB + s * Ly.stage_b + k * kChunkN * kRowBytes +
+                                        h * kTileM * kRowBytes,
+                                    &tmap, k * 64, row + h * kTileM, bar(kBarFull + s));
                 issued = c + 1;
             }
             DC_PROF_STORE(4, w_a);
@@ -319,7 +329,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else {
                 tc_fence_after();
                 const int ksteps = P.atoms * 4;  // 16 elements (32 bytes) per MMA
+                int lv = 0;
                 for (int c = 0; c < nchunks; c++) {
+                    while (c >= sched[lv].first + sched[lv].count) lv++;
                     const int s = c % kStagesB, a = c % kAcc;
                     const long long t0 = DC_PROF_NOW();
                     if (!mbar_wait(bar(kBarFull + s), (c / kStagesB) & 1, abort)) {
@@ -334,7 +346,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     w_b += DC_PROF_NOW() - t1;
                     tc_fence_after();
-                    const uint32_t idesc = idesc_f16(P.ab_fmt, kTileM, chunks[c].n);
+                    const int n = make_chunk(sched[lv], c - sched[lv].first, 0).n;
+                    const uint32_t idesc = idesc_f16(P.ab_fmt, kTileM, n);
                     const uint32_t d = tmem + (uint32_t)(a * kChunkN);
                     for (int kk = 0; kk < ksteps; kk++) {
                         const int at = kk >> 2, wi = kk & 3;
@@ -372,7 +385,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int ylo = max(by, 0), yhi = min(by + NW - 1, Hl - 1);
             const int xlo = max(bx, 0), xhi = min(bx + NW - 1, Wl - 1);
             const bool any = pv && ylo <= yhi && xlo <= xhi;
-            while (c < nchunks && chunks[c].level == l) {
+            const float inv_seg_max = 1.0f / (float)sched[l].seg_max;
+            const LevelSched Ls = sched[l];
+            for (; c < Ls.first + Ls.count; c++) {
                 const int a = c % kAcc;
                 const uint32_t par = (c / kAcc) & 1;
                 const long long t0 = DC_PROF_NOW();
@@ -394,14 +409,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
                 const long long t1 = DC_PROF_NOW();
                 w_a += t1 - t0;
-                const ChunkDesc& ch = chunks[c];
+                const ChunkDesc ch = make_chunk(Ls, c - Ls.first, 0);
+                const float inv_seg = ch.seg == Ls.seg_max ? inv_seg_max : 1.0f / (float)ch.seg;
 #pragma unroll
                 for (int pass = 0; pass < kPasses; pass++) {
                 const int cb = cwarp + kSubCols * pass;
-                    const int qi = cb / kSubCols;
-                    if (ch.rhi[qi] >= 0) {
-                        const int rlo = ch.rlo[qi];
-                        const int rhi = ch.rhi[qi];
+                    if (cb < ch.cols) {
+                        const int rlo = div_small(cb, inv_seg);
+                        const int rhi = div_small(min(ch.cols - 1, cb + kSubCols - 1), inv_seg);
                         // window rows of this pixel inside this warp's chunk rows
                         const int ya = max(ylo, ch.y0 + rlo);
                         const int yb = min(yhi, ch.y0 + rhi);
@@ -449,7 +464,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(bar(kBarTEmpty + a));
-                c++;
                 w_b += DC_PROF_NOW() - t1;
             }
             if (!alive) break;
@@ -554,7 +568,7 @@ int dc_tc_prepare(dc_ctx* ctx) {
                           (cuuint64_t)ctx->cfg.max_frames * ctx->frame_rows};
     cuuint64_t strides[1] = {(cuuint64_t)ctx->cfg.channels * 2};
     cuuint32_t estr[2] = {1, 1};
-    static_assert(kTileM == kChunkN, "one box shape serves A tiles and B chunks");
+    static_assert(kChunkN % kTileM == 0, "B chunks are whole 128-row boxes");
     cuuint32_t box[2] = {64, (cuuint32_t)kTileM};
     CUresult r1 = enc(reinterpret_cast<CUtensorMap*>(ctx->tmap_a), dt, 2, ctx->store, dims,
                       strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
