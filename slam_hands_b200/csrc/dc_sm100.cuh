@@ -58,7 +58,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
     const uint64_t t0 = globaltimer();
     for (uint32_t it = 1;; it++) {
         if (mbar_try_wait(bar, parity)) return true;
-        __nanosleep(32);  // back off: spinning warps would take issue slots
+        __nanosleep(128);  // back off: spinning warps would take issue slots
         if ((it & 255u) == 0) {
             if (abort && *abort) return false;
             if (globaltimer() - t0 > limit_ns) return false;

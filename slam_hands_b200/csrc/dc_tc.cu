@@ -478,16 +478,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // the quarter's warps split the output columns a: 2, 2, 2, 1 (R = 3)
                 constexpr int AW = (D + kSubWarps - 1) / kSubWarps;  // columns per warp
                 const int a0 = sub * AW;
-                // taps of columns a0 .. a0 + AW (registers indexed statically)
-                float tv[AW + 1][NW];
-                bool vxa[AW + 1];
+                // taps of columns a0 .. a0 + AW (registers indexed statically);
+                // taps outside the level read as +0, which leaves every fmaf
+                // below unchanged, as skipping them does in the reference
+                float pu[AW + 1][NW], pd[AW + 1][NW];  // s * (1 - dx), s * dx
 #pragma unroll
                 for (int ii = 0; ii <= AW; ii++) {
                     const int i = a0 + ii;
-                    vxa[ii] = i < NW && (unsigned)(bx + i) < (unsigned)Wl;
+                    const bool vx = i < NW && (unsigned)(bx + i) < (unsigned)Wl;
 #pragma unroll
-                    for (int j = 0; j < NW; j++)
-                        tv[ii][j] = (vxa[ii] && vy[j]) ? win[i * 8 + j] : 0.0f;
+                    for (int j = 0; j < NW; j++) {
+                        const float t = (vx && vy[j]) ? win[i * 8 + j] : 0.0f;
+                        pu[ii][j] = t * ux;
+                        pd[ii][j] = t * dx;
+                    }
                 }
 #pragma unroll
                 for (int ai = 0; ai < AW; ai++) {
@@ -495,11 +499,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (a >= D) break;
 #pragma unroll
                     for (int b = 0; b < D; b++) {
-                        float acc = 0.0f;
-                        acc = dc::bilinear_tap(acc, tv[ai][b], vxa[ai] && vy[b], ux, uy);
-                        acc = dc::bilinear_tap(acc, tv[ai][b + 1], vxa[ai] && vy[b + 1], ux, dy);
-                        acc = dc::bilinear_tap(acc, tv[ai + 1][b], vxa[ai + 1] && vy[b], dx, uy);
-                        acc = dc::bilinear_tap(acc, tv[ai + 1][b + 1], vxa[ai + 1] && vy[b + 1], dx, dy);
+                        // reference order: taps (a,b), (a,b+1), (a+1,b), (a+1,b+1)
+                        float acc = fmaf(pu[ai][b], uy, 0.0f);
+                        acc = fmaf(pu[ai][b + 1], dy, acc);
+                        acc = fmaf(pd[ai + 1][b], uy, acc);
+                        acc = fmaf(pd[ai + 1][b + 1], dy, acc);
                         __stcs(ol + (size_t)(a * D + b) * hw, acc);
                     }
                 }
