@@ -100,10 +100,15 @@ struct TcParams {
     int* err;
     int atoms;        // 128-byte K atoms per operand row (C * 2 / 128)
     uint32_t ab_fmt;  // 0 fp16, 1 bf16
+    int M;            // edges
+};
+
+struct TileInfo {
+    int e, p0, si, sj, n, valid, pad0, pad1;
 };
 
 struct Layout {
-    uint32_t a, b, stage_b, win, st, chunks, bars, misc, total;
+    uint32_t a, b, stage_b, win, st, sched, tinfo, coords, bars, misc, total;
 };
 
 __host__ __device__ constexpr Layout make_layout(int atoms) {
@@ -113,8 +118,10 @@ __host__ __device__ constexpr Layout make_layout(int atoms) {
     L.stage_b = atoms * kChunkN * kRowBytes;
     L.win = L.b + kStagesB * L.stage_b;
     L.st = L.win + kTileM * kWinStride * 4;
-    L.chunks = L.st + kEpiWarps * 32 * kStStride * 4;
-    L.bars = L.chunks + DC_MAX_LEVELS * sizeof(LevelSched);
+    L.sched = L.st + kEpiWarps * 32 * kStStride * 4;       // [2][levels] LevelSched
+    L.tinfo = L.sched + 2 * DC_MAX_LEVELS * sizeof(LevelSched);
+    L.coords = L.tinfo + 2 * sizeof(TileInfo);              // [2][2][128] floats
+    L.bars = L.coords + 2 * 2 * kTileM * 4;
     L.misc = L.bars + 24 * 8;
     L.total = L.misc + 64;
     return L;
@@ -122,11 +129,13 @@ __host__ __device__ constexpr Layout make_layout(int atoms) {
 static_assert(make_layout(2).total + 1024 <= 227 * 1024, "shared memory budget");
 
 // misc words
-enum { kMiscTmem = 0, kMiscAbort = 1, kMiscCount = 2, kMiscRange = 4 };  // range: 2 per level
-// barrier slots
-enum { kBarA = 0, kBarFull = 1, kBarEmpty = kBarFull + kStagesB,
-       kBarTFull = kBarEmpty + kStagesB, kBarTEmpty = kBarTFull + kAcc };
-static_assert(kBarTEmpty + kAcc <= 24, "barrier slots");
+enum { kMiscTmem = 0, kMiscAbort = 1 };
+// barrier slots: A tile full/empty, B stages full/empty, TMEM accumulators
+// full/empty, per-tile schedule full/empty (double-buffered by tile parity)
+enum { kBarAFull = 0, kBarAEmpty = 1, kBarFull = 2, kBarEmpty = kBarFull + kStagesB,
+       kBarTFull = kBarEmpty + kStagesB, kBarTEmpty = kBarTFull + kAcc,
+       kBarSFull = kBarTEmpty + kAcc, kBarSEmpty = kBarSFull + 2 };
+static_assert(kBarSEmpty + 2 <= 24, "barrier slots");
 
 __device__ __forceinline__ void raise_abort(volatile int* abort, int* err, int code) {
     *abort = 1;
@@ -134,14 +143,13 @@ __device__ __forceinline__ void raise_abort(volatile int* abort, int* err, int c
 }
 
 // Optional phase timers (build with -DDC_TC_PROFILE; compiled out otherwise):
-// per CTA, cycles spent in set-up, in each role's waits and in the epilogue
-// phases, for tuning the pipeline.
+// per CTA, cycles spent in each role's waits and in the epilogue phases.
 #ifdef DC_TC_PROFILE
 __device__ unsigned long long g_tc_prof[8192 * 16];
 #define DC_PROF_NOW() clock64()
 #define DC_PROF_STORE(slot, v)                                                    \
     do {                                                                          \
-        const int cta_ = blockIdx.y * gridDim.x + blockIdx.x;                     \
+        const int cta_ = blockIdx.x;                                              \
         if (cta_ < 8192) g_tc_prof[cta_ * 16 + (slot)] = (unsigned long long)(v); \
     } while (0)
 #else
@@ -156,6 +164,21 @@ __device__ __forceinline__ void quarter_sync(int quarter) {
     asm volatile("bar.sync %0, %1;" ::"r"(1 + quarter), "r"(32 * kSubWarps) : "memory");
 }
 
+// All lanes of a warp wait for one barrier phase: lane 0 polls (bounded), the
+// others then observe the completed phase.  Returns false on a time-out.
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort,
+                                          int lane) {
+    int ok = 1;
+    if (lane == 0) ok = mbar_wait(bar, parity, abort) ? 1 : 0;
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    if (ok) mbar_wait(bar, parity, abort);
+    return ok != 0;
+}
+
+// Persistent: CTA b handles tiles b, b + gridDim.x, ...; tile t = (edge t / tpe,
+// source pixels 128 * (t % tpe) ..).  The producer warp also prepares each
+// tile's coordinates and chunk schedule one tile ahead, so a tile's set-up and
+// its last level's bilinear step overlap the neighbouring tiles' MMAs.
 template <int R>
 __global__ void __launch_bounds__(kThreads, 1)
     corr_tc_kernel(const __grid_constant__ CUtensorMap tmap, TcParams P) {
@@ -167,45 +190,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     const Layout Ly = P.atoms == 2 ? Ly2 : make_layout(P.atoms);
     const dc::Geom& g = P.g;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int e = blockIdx.y, p0 = blockIdx.x * kTileM;
     const int hw = g.hw, nch = g.levels * D * D;
-    float* out_e = P.out + (size_t)e * nch * hw;
+    const int tpe = (hw + kTileM - 1) / kTileM;  // tiles per edge
+    const int ntiles = tpe * P.M;
     const long long t_start = DC_PROF_NOW();
     (void)t_start;
-
-    const int si = P.ii[e], sj = P.jj[e];
-    if (!(si >= 0 && si < P.max_frames && sj >= 0 && sj < P.max_frames)) {
-        for (int idx = threadIdx.x; idx < nch * kTileM; idx += kThreads) {
-            const int p = p0 + (idx % kTileM);
-            if (p < hw) out_e[(size_t)(idx / kTileM) * hw + p] = 0.0f;
-        }
-        return;
-    }
 
     const uint32_t sA = smem_addr(base + Ly.a);
     const uint32_t sB = smem_addr(base + Ly.b);
     float* win_base = reinterpret_cast<float*>(base + Ly.win);
     float* st_base = reinterpret_cast<float*>(base + Ly.st);
-    LevelSched* sched = reinterpret_cast<LevelSched*>(base + Ly.chunks);
+    LevelSched* sched_base = reinterpret_cast<LevelSched*>(base + Ly.sched);
+    TileInfo* tinfo = reinterpret_cast<TileInfo*>(base + Ly.tinfo);
+    float* scoords = reinterpret_cast<float*>(base + Ly.coords);
     const uint32_t bars = smem_addr(base + Ly.bars);
     int* misc = reinterpret_cast<int*>(base + Ly.misc);
     volatile int* abort = misc + kMiscAbort;
     auto bar = [&](int slot) { return bars + 8u * slot; };
 
-    const bool epi = warp >= 2;
-    const int quarter = warp & 3;            // TMEM lane quarter of this warp
-    const int sub = (warp - 2) >> 2;         // which 32-column slice of a chunk (0..3)
-    const int ti = 32 * quarter + lane;      // tile pixel (epilogue threads)
-    const int p = p0 + ti;
-    const bool pv = epi && p < hw;
-    float cx = 0.0f, cy = 0.0f;
-    if (pv) {
-        cx = __ldg(P.coords + (size_t)e * 2 * hw + p);
-        cy = __ldg(P.coords + (size_t)e * 2 * hw + hw + p);
-    }
-
     if (threadIdx.x == 0) {
-        mbar_init(bar(kBarA), 1);
+        mbar_init(bar(kBarAFull), 1);
+        mbar_init(bar(kBarAEmpty), 1);
         for (int s = 0; s < kStagesB; s++) {
             mbar_init(bar(kBarFull + s), 1);
             mbar_init(bar(kBarEmpty + s), 1);
@@ -214,11 +219,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(bar(kBarTFull + a), 1);
             mbar_init(bar(kBarTEmpty + a), kEpiWarps);
         }
-        misc[kMiscAbort] = 0;
-        for (int l = 0; l < DC_MAX_LEVELS; l++) {
-            misc[kMiscRange + 2 * l] = 0x7fffffff;
-            misc[kMiscRange + 2 * l + 1] = -1;
+        for (int b = 0; b < 2; b++) {
+            mbar_init(bar(kBarSFull + b), 1);
+            mbar_init(bar(kBarSEmpty + b), kEpiWarps + 1);
         }
+        misc[kMiscAbort] = 0;
         fence_mbar_init();
         tma_prefetch_desc(&tmap);
     }
@@ -230,291 +235,358 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = (uint32_t)misc[kMiscTmem];
-
-    // the source tile does not depend on the windows: start its load now
-    if (threadIdx.x == 0) {
-        mbar_arrive_expect_tx(bar(kBarA), P.atoms * kTileM * kRowBytes);
-        const int arow = (int)((long long)si * g.frame_rows + g.row0[0] + p0);
-        for (int k = 0; k < P.atoms; k++)
-            tma_load_2d(sA + k * kTileM * kRowBytes, &tmap, k * 64, arow, bar(kBarA));
-    }
-
-    // ---- 1. target-row range per level over this tile's windows
-    if (epi && sub == 0) {
-        for (int l = 0; l < g.levels; l++) {
-            const float sc = 1.0f / (float)(1 << l);
-            const int by = (int)floorf(cy * sc) - R, bx = (int)floorf(cx * sc) - R;
-            int lo = max(by, 0), hi = min(by + NW - 1, g.H[l] - 1);
-            const bool xin = bx + NW - 1 >= 0 && bx < g.W[l];
-            if (!(pv && lo <= hi && xin)) {
-                lo = 0x7fffffff;
-                hi = -1;
-            }
-            lo = __reduce_min_sync(0xffffffffu, lo);
-            hi = __reduce_max_sync(0xffffffffu, hi);
-            if (lane == 0 && lo <= hi) {
-                atomicMin(&misc[kMiscRange + 2 * l], lo);
-                atomicMax(&misc[kMiscRange + 2 * l + 1], hi);
-            }
-        }
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        int n = 0;
-        for (int l = 0; l < DC_MAX_LEVELS; l++) {
-            LevelSched L;
-            L.first = n;
-            L.count = 0;
-            L.ylo = misc[kMiscRange + 2 * l];
-            L.yhi = misc[kMiscRange + 2 * l + 1];
-            L.W = max(g.W[l], 1);
-            L.rows_per = L.W <= kChunkN ? kChunkN / L.W : 1;
-            L.seg_max = L.W <= kChunkN ? L.W : kChunkN;
-            L.segs = (L.W + L.seg_max - 1) / L.seg_max;
-            if (l < g.levels && L.ylo <= L.yhi)
-                L.count = (L.yhi - L.ylo + L.rows_per) / L.rows_per * L.segs;
-            n += L.count;
-            sched[l] = L;
-        }
-        misc[kMiscCount] = n;
-    }
-    __syncthreads();
-    const int nchunks = misc[kMiscCount];
-    if (threadIdx.x == 0) {
-        DC_PROF_STORE(1, DC_PROF_NOW() - t_start);
-        DC_PROF_STORE(8, nchunks);
-    }
-    long long w_a = 0, w_b = 0, w_c = 0;  // per-role phase cycles (profiling builds)
+    long long w_a = 0, w_b = 0, w_c = 0;  // phase cycles (profiling builds)
 
     if (warp == 0) {
-        // ---- 2. TMA producer
-        if (lane == 0) {
-            const uint32_t b_bytes = Ly.stage_b;
-            int issued = 0;
-            int lv = 0;
-            for (int c = 0; c < nchunks; c++) {
-                while (c >= sched[lv].first + sched[lv].count) lv++;
-                const int s = c % kStagesB;
-                const long long t0 = DC_PROF_NOW();
-                if (c >= kStagesB &&
-                    !mbar_wait(bar(kBarEmpty + s), ((c / kStagesB) - 1) & 1, abort)) {
-                    raise_abort(abort, P.err, 1);
-                    break;
-                }
-                w_a += DC_PROF_NOW() - t0;
-                mbar_arrive_expect_tx(bar(kBarFull + s), b_bytes);
-                const int row = make_chunk(sched[lv], c - sched[lv].first,
-                                           (long long)sj * g.frame_rows + g.row0[lv]).row;
-                for (int k = 0; k < P.atoms; k++)
-                    for (int h = 0; h < kChunkN / kTileM; h++)  // boxes of 128 rows
-                        tma_load_2d(sB + s * Ly.stage_b + k * kChunkN * kRowBytes +
-                                        h * kTileM * kRowBytes,
-                                    &tmap, k * 64, row + h * kTileM, bar(kBarFull + s));
-                issued = c + 1;
+        // ---- producer: per tile, coordinates + chunk schedule, then the source
+        //      tile and the target-row chunks through TMA
+        int gc = 0, na = 0, i = 0;
+        int a_issued = 0, last_gc = 0;
+        for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x, i++) {
+            const int tb = i & 1;
+            if (i >= 2 && !warp_wait(bar(kBarSEmpty + tb), ((i >> 1) - 1) & 1, abort, lane)) {
+                if (lane == 0) raise_abort(abort, P.err, 1);
+                break;
             }
+            const int e = t / tpe, p0 = (t - e * tpe) * kTileM;
+            const int si = P.ii[e], sj = P.jj[e];
+            const bool valid = si >= 0 && si < P.max_frames && sj >= 0 && sj < P.max_frames;
+            float* sc = scoords + tb * 2 * kTileM;
+            int lo[DC_MAX_LEVELS], hi[DC_MAX_LEVELS];
+#pragma unroll
+            for (int l = 0; l < DC_MAX_LEVELS; l++) {
+                lo[l] = 0x7fffffff;
+                hi[l] = -1;
+            }
+#pragma unroll
+            for (int k = 0; k < kTileM / 32; k++) {
+                const int q = lane + 32 * k, p = p0 + q;
+                float cx = 0.0f, cy = 0.0f;
+                if (p < hw) {
+                    cx = __ldg(P.coords + (size_t)e * 2 * hw + p);
+                    cy = __ldg(P.coords + (size_t)e * 2 * hw + hw + p);
+                }
+                sc[q] = cx;
+                sc[kTileM + q] = cy;
+                if (!(valid && p < hw)) continue;
+#pragma unroll
+                for (int l = 0; l < DC_MAX_LEVELS; l++) {
+                    if (l >= g.levels) break;
+                    const float s = 1.0f / (float)(1 << l);
+                    const int by = (int)floorf(cy * s) - R, bx = (int)floorf(cx * s) - R;
+                    const int a0 = max(by, 0), a1 = min(by + NW - 1, g.H[l] - 1);
+                    if (a0 <= a1 && bx + NW - 1 >= 0 && bx < g.W[l]) {
+                        lo[l] = min(lo[l], a0);
+                        hi[l] = max(hi[l], a1);
+                    }
+                }
+            }
+            int n = 0;
+#pragma unroll
+            for (int l = 0; l < DC_MAX_LEVELS; l++) {
+                const int ylo = __reduce_min_sync(0xffffffffu, lo[l]);
+                const int yhi = __reduce_max_sync(0xffffffffu, hi[l]);
+                LevelSched L;
+                L.first = n;
+                L.count = 0;
+                L.ylo = ylo;
+                L.yhi = yhi;
+                L.W = max(g.W[l], 1);
+                L.rows_per = L.W <= kChunkN ? kChunkN / L.W : 1;
+                L.seg_max = L.W <= kChunkN ? L.W : kChunkN;
+                L.segs = (L.W + L.seg_max - 1) / L.seg_max;
+                if (l < g.levels && ylo <= yhi)
+                    L.count = (yhi - ylo + L.rows_per) / L.rows_per * L.segs;
+                n += L.count;
+                if (lane == 0) sched_base[tb * DC_MAX_LEVELS + l] = L;
+            }
+            if (lane == 0) {
+                TileInfo ti;
+                ti.e = e;
+                ti.p0 = p0;
+                ti.si = si;
+                ti.sj = sj;
+                ti.n = n;
+                ti.valid = valid;
+                ti.pad0 = ti.pad1 = 0;
+                tinfo[tb] = ti;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(kBarSFull + tb));  // release: schedule, coords
+            if (n == 0) continue;
+            if (lane == 0) {
+                // the single source-tile buffer: wait until the MMAs of the previous
+                // tile that used it are done
+                if (na >= 1 && !mbar_wait(bar(kBarAEmpty), (na - 1) & 1, abort)) {
+                    raise_abort(abort, P.err, 2);
+                } else {
+                    mbar_arrive_expect_tx(bar(kBarAFull), P.atoms * kTileM * kRowBytes);
+                    const int arow = (int)((long long)si * g.frame_rows + g.row0[0] + p0);
+                    for (int k = 0; k < P.atoms; k++)
+                        tma_load_2d(sA + k * kTileM * kRowBytes, &tmap, k * 64, arow,
+                                    bar(kBarAFull));
+                    a_issued = 1;
+                    const LevelSched* sch = sched_base + tb * DC_MAX_LEVELS;
+                    int lv = 0;
+                    for (int c = 0; c < n; c++, gc++) {
+                        while (c >= sch[lv].first + sch[lv].count) lv++;
+                        const int s = gc % kStagesB;
+                        const long long t0 = DC_PROF_NOW();
+                        if (gc >= kStagesB &&
+                            !mbar_wait(bar(kBarEmpty + s), ((gc / kStagesB) - 1) & 1, abort)) {
+                            raise_abort(abort, P.err, 3);
+                            break;
+                        }
+                        w_a += DC_PROF_NOW() - t0;
+                        mbar_arrive_expect_tx(bar(kBarFull + s), Ly.stage_b);
+                        const int row = make_chunk(sch[lv], c - sch[lv].first,
+                                                   (long long)sj * g.frame_rows + g.row0[lv]).row;
+                        for (int k = 0; k < P.atoms; k++)
+                            for (int h = 0; h < kChunkN / kTileM; h++)  // 128-row boxes
+                                tma_load_2d(sB + s * Ly.stage_b + k * kChunkN * kRowBytes +
+                                                h * kTileM * kRowBytes,
+                                            &tmap, k * 64, row + h * kTileM, bar(kBarFull + s));
+                        last_gc = gc + 1;
+                    }
+                }
+            }
+            na++;
+            __syncwarp();
+        }
+        if (lane == 0) {
             DC_PROF_STORE(4, w_a);
             if (*abort) {
                 // let this CTA's copies in flight land before the CTA exits
-                mbar_wait(bar(kBarA), 0, nullptr);
-                for (int c = max(0, issued - kStagesB); c < issued; c++)
+                if (a_issued) mbar_wait(bar(kBarAFull), (na - 1) & 1, nullptr);
+                for (int c = max(0, last_gc - kStagesB); c < last_gc; c++)
                     mbar_wait(bar(kBarFull + c % kStagesB), (c / kStagesB) & 1, nullptr);
             }
         }
         __syncwarp();
     } else if (warp == 1) {
-        // ---- 3. MMA issuer
-        if (lane == 0) {
-            if (!mbar_wait(bar(kBarA), 0, abort)) {
-                raise_abort(abort, P.err, 2);
-            } else {
-                tc_fence_after();
-                const int ksteps = P.atoms * 4;  // 16 elements (32 bytes) per MMA
-                int lv = 0;
-                for (int c = 0; c < nchunks; c++) {
-                    while (c >= sched[lv].first + sched[lv].count) lv++;
-                    const int s = c % kStagesB, a = c % kAcc;
-                    const long long t0 = DC_PROF_NOW();
-                    if (!mbar_wait(bar(kBarFull + s), (c / kStagesB) & 1, abort)) {
-                        raise_abort(abort, P.err, 3);
-                        break;
-                    }
-                    const long long t1 = DC_PROF_NOW();
-                    w_a += t1 - t0;
-                    if (c >= kAcc && !mbar_wait(bar(kBarTEmpty + a), ((c / kAcc) - 1) & 1, abort)) {
-                        raise_abort(abort, P.err, 4);
-                        break;
-                    }
-                    w_b += DC_PROF_NOW() - t1;
-                    tc_fence_after();
-                    const int n = make_chunk(sched[lv], c - sched[lv].first, 0).n;
-                    const uint32_t idesc = idesc_f16(P.ab_fmt, kTileM, n);
-                    const uint32_t d = tmem + (uint32_t)(a * kChunkN);
-                    for (int kk = 0; kk < ksteps; kk++) {
-                        const int at = kk >> 2, wi = kk & 3;
-                        const uint64_t ad = sdesc_sw128(sA + at * kTileM * kRowBytes + wi * 32);
-                        const uint64_t bd =
-                            sdesc_sw128(sB + s * Ly.stage_b + at * kChunkN * kRowBytes + wi * 32);
-#if !(defined(DC_TC_EXP) && DC_TC_EXP == 4)
-                        mma_f16(d, ad, bd, idesc, kk > 0 ? 1u : 0u);
-#endif
-                    }
-                    mma_commit(bar(kBarEmpty + s));
-                    mma_commit(bar(kBarTFull + a));
-                }
-                DC_PROF_STORE(2, w_a);
-                DC_PROF_STORE(3, w_b);
+        // ---- MMA issuer
+        int gc = 0, na = 0, i = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, i++) {
+            const int tb = i & 1;
+            if (!warp_wait(bar(kBarSFull + tb), (i >> 1) & 1, abort, lane)) {
+                if (lane == 0) raise_abort(abort, P.err, 4);
+                break;
             }
+            const TileInfo ti = tinfo[tb];
+            const LevelSched* sch = sched_base + tb * DC_MAX_LEVELS;
+            bool ok = true;
+            if (lane == 0 && ti.n > 0) {
+                if (!mbar_wait(bar(kBarAFull), na & 1, abort)) {
+                    raise_abort(abort, P.err, 5);
+                    ok = false;
+                } else {
+                    tc_fence_after();
+                    const int ksteps = P.atoms * 4;  // 16 elements (32 bytes) per MMA
+                    int lv = 0;
+                    for (int c = 0; c < ti.n; c++, gc++) {
+                        while (c >= sch[lv].first + sch[lv].count) lv++;
+                        const int s = gc % kStagesB, a = gc % kAcc;
+                        const long long t0 = DC_PROF_NOW();
+                        if (!mbar_wait(bar(kBarFull + s), (gc / kStagesB) & 1, abort)) {
+                            raise_abort(abort, P.err, 6);
+                            ok = false;
+                            break;
+                        }
+                        const long long t1 = DC_PROF_NOW();
+                        w_a += t1 - t0;
+                        if (gc >= kAcc &&
+                            !mbar_wait(bar(kBarTEmpty + a), ((gc / kAcc) - 1) & 1, abort)) {
+                            raise_abort(abort, P.err, 7);
+                            ok = false;
+                            break;
+                        }
+                        w_b += DC_PROF_NOW() - t1;
+                        tc_fence_after();
+                        const int nn = make_chunk(sch[lv], c - sch[lv].first, 0).n;
+                        const uint32_t idesc = idesc_f16(P.ab_fmt, kTileM, nn);
+                        const uint32_t d = tmem + (uint32_t)(a * kChunkN);
+                        for (int kk = 0; kk < ksteps; kk++) {
+                            const int at = kk >> 2, wi = kk & 3;
+                            const uint64_t ad = sdesc_sw128(sA + at * kTileM * kRowBytes + wi * 32);
+                            const uint64_t bd = sdesc_sw128(sB + s * Ly.stage_b +
+                                                            at * kChunkN * kRowBytes + wi * 32);
+                            mma_f16(d, ad, bd, idesc, kk > 0 ? 1u : 0u);
+                        }
+                        mma_commit(bar(kBarEmpty + s));
+                        mma_commit(bar(kBarTFull + a));
+                    }
+                    mma_commit(bar(kBarAEmpty));  // the source tile may be replaced
+                }
+            }
+            if (ti.n > 0) na++;
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            if (lane == 0) mbar_arrive(bar(kBarSEmpty + tb));
+            if (!ok) break;
+        }
+        if (lane == 0) {
+            DC_PROF_STORE(2, w_a);
+            DC_PROF_STORE(3, w_b);
         }
         __syncwarp();
     } else {
-        // ---- 4. epilogue: the two warps of a lane quarter take the two
-        //         64-column halves of each chunk
-        float* win = win_base + ti * kWinStride;
+        // ---- epilogue: the kSubWarps warps of a TMEM lane quarter take the
+        //      32-column passes of each chunk and split the outputs
+        const int quarter = warp & 3;       // TMEM lane quarter of this warp
+        const int sub = (warp - 2) >> 2;    // which columns of a chunk (0..kSubWarps-1)
+        const int ti_px = 32 * quarter + lane;
+        float* win = win_base + ti_px * kWinStride;
         float* st = st_base + ((warp - 2) * 32 + lane) * kStStride;
         const uint32_t tl = tmem + ((uint32_t)(32 * quarter) << 16);
         const int cwarp = kSubCols * kPasses * sub;  // first chunk column of this warp
-        int c = 0;
+        int gc = 0, i = 0;
         bool alive = true;
-        for (int l = 0; l < g.levels && alive; l++) {
-            const int Hl = g.H[l], Wl = g.W[l];
-            const float scale = 1.0f / (float)(1 << l);
-            const float x0 = cx * scale, y0 = cy * scale;
-            const float fx = floorf(x0), fy = floorf(y0);
-            const float dx = x0 - fx, dy = y0 - fy;
-            const int bx = (int)fx - R, by = (int)fy - R;
-            const int ylo = max(by, 0), yhi = min(by + NW - 1, Hl - 1);
-            const int xlo = max(bx, 0), xhi = min(bx + NW - 1, Wl - 1);
-            const bool any = pv && ylo <= yhi && xlo <= xhi;
-            const float inv_seg_max = 1.0f / (float)sched[l].seg_max;
-            const LevelSched Ls = sched[l];
-            for (; c < Ls.first + Ls.count; c++) {
-                const int a = c % kAcc;
-                const uint32_t par = (c / kAcc) & 1;
-                const long long t0 = DC_PROF_NOW();
-                int okw = 1;
-#if defined(DC_TC_EXP) && DC_TC_EXP == 3
-                (void)par;
-#else
-                if (lane == 0) okw = mbar_wait(bar(kBarTFull + a), par, abort) ? 1 : 0;
-#endif
-                okw = __shfl_sync(0xffffffffu, okw, 0);
-                if (!okw) {
-                    if (lane == 0) raise_abort(abort, P.err, 5);
-                    alive = false;
-                    break;
-                }
-#if !(defined(DC_TC_EXP) && DC_TC_EXP == 3)
-                mbar_wait(bar(kBarTFull + a), par, abort);
-#endif
-                tc_fence_after();
-                const long long t1 = DC_PROF_NOW();
-                w_a += t1 - t0;
-                const ChunkDesc ch = make_chunk(Ls, c - Ls.first, 0);
-                const float inv_seg = ch.seg == Ls.seg_max ? inv_seg_max : 1.0f / (float)ch.seg;
+        for (int t = blockIdx.x; t < ntiles && alive; t += gridDim.x, i++) {
+            const int tb = i & 1;
+            const long long t0s = DC_PROF_NOW();
+            if (!warp_wait(bar(kBarSFull + tb), (i >> 1) & 1, abort, lane)) {
+                if (lane == 0) raise_abort(abort, P.err, 8);
+                break;
+            }
+            w_a += DC_PROF_NOW() - t0s;
+            const TileInfo tinf = tinfo[tb];
+            const LevelSched* sch = sched_base + tb * DC_MAX_LEVELS;
+            const int p = tinf.p0 + ti_px;
+            const bool pv = p < hw;
+            const bool valid = tinf.valid != 0;
+            const float cx = scoords[tb * 2 * kTileM + ti_px];
+            const float cy = scoords[tb * 2 * kTileM + kTileM + ti_px];
+            float* out_e = P.out + (size_t)tinf.e * nch * hw;
+            int cend = 0;
+            for (int l = 0; l < g.levels && alive; l++) {
+                const int Hl = g.H[l], Wl = g.W[l];
+                const float scale = 1.0f / (float)(1 << l);
+                const float x0 = cx * scale, y0 = cy * scale;
+                const float fx = floorf(x0), fy = floorf(y0);
+                const float dx = x0 - fx, dy = y0 - fy;
+                const int bx = (int)fx - R, by = (int)fy - R;
+                const int ylo = max(by, 0), yhi = min(by + NW - 1, Hl - 1);
+                const int xlo = max(bx, 0), xhi = min(bx + NW - 1, Wl - 1);
+                const bool any = valid && pv && ylo <= yhi && xlo <= xhi;
+                const LevelSched Ls = sch[l];
+                const float inv_seg_max = 1.0f / (float)Ls.seg_max;
+                cend += Ls.count;
+                for (int c = 0; c < Ls.count; c++, gc++) {
+                    const int a = gc % kAcc;
+                    const long long t0 = DC_PROF_NOW();
+                    if (!warp_wait(bar(kBarTFull + a), (gc / kAcc) & 1, abort, lane)) {
+                        if (lane == 0) raise_abort(abort, P.err, 9);
+                        alive = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const long long t1 = DC_PROF_NOW();
+                    w_a += t1 - t0;
+                    const ChunkDesc ch = make_chunk(Ls, c, 0);
+                    const float inv_seg =
+                        ch.seg == Ls.seg_max ? inv_seg_max : 1.0f / (float)ch.seg;
 #pragma unroll
-                for (int pass = 0; pass < kPasses; pass++) {
-                const int cb = cwarp + kSubCols * pass;
-                    if (cb < ch.cols) {
+                    for (int pass = 0; pass < kPasses; pass++) {
+                        const int cb = cwarp + kSubCols * pass;
+                        if (cb >= ch.cols) continue;
                         const int rlo = div_small(cb, inv_seg);
                         const int rhi = div_small(min(ch.cols - 1, cb + kSubCols - 1), inv_seg);
-                        // window rows of this pixel inside this warp's chunk rows
+                        // window rows of this pixel inside this pass's chunk rows; tap
+                        // (x, y) sits at staged column (y - y0) * seg + (x - x0) - cb
                         const int ya = max(ylo, ch.y0 + rlo);
                         const int yb = min(yhi, ch.y0 + rhi);
-                        // this pixel's taps in staged-column coordinates: row y, tap x
-                        // sits at column (y - y0) * seg + (x - x0) - cb
                         const int xa = max(xlo, ch.x0), xb = min(xhi, ch.x0 + ch.seg - 1);
                         const bool need = any && ya <= yb && xa <= xb;
-                        if (__any_sync(0xffffffffu, need)) {
-                            float v[kSubCols];
-                            tmem_ld32(tl + (uint32_t)(a * kChunkN + cb), v);
-                            if (need) {
-                                const int kofs = -ch.x0 - cb;
-                                // valid taps i of a row: x = bx + i in [xa, xb] and staged
-                                // column k0 + i in [0, 32); branch-free predicates
-                                const int ia = xa - bx, ib = xb - bx;
-                                for (int y = ya; y <= yb; y++) {
-                                    const int k0 = (y - ch.y0) * ch.seg + bx + kofs;
-                                    const int lo = max(ia, -k0), hi = min(ib, kSubCols - 1 - k0);
-                                    if (lo > hi) continue;
-                                    const unsigned span = (unsigned)(hi - lo);
-                                    // stage the <= 3 16-byte groups holding this row's taps,
-                                    // compacted: group g goes to slot g - g0
-                                    const int g0 = (k0 + lo) >> 2;
-                                    const unsigned gspan = (unsigned)(((k0 + hi) >> 2) - g0);
-                                    float4* st4 = reinterpret_cast<float4*>(st);
+                        if (!__any_sync(0xffffffffu, need)) continue;
+                        float v[kSubCols];
+                        tmem_ld32(tl + (uint32_t)(a * kChunkN + cb), v);
+                        if (!need) continue;
+                        const int kofs = -ch.x0 - cb;
+                        const int ia = xa - bx, ib = xb - bx;  // valid tap range
+                        for (int y = ya; y <= yb; y++) {
+                            const int k0 = (y - ch.y0) * ch.seg + bx + kofs;
+                            const int lo = max(ia, -k0), hi = min(ib, kSubCols - 1 - k0);
+                            if (lo > hi) continue;
+                            const unsigned span = (unsigned)(hi - lo);
+                            // stage the <= 3 16-byte groups holding this row's taps,
+                            // compacted: group g goes to slot g - g0
+                            const int g0 = (k0 + lo) >> 2;
+                            const unsigned gspan = (unsigned)(((k0 + hi) >> 2) - g0);
+                            float4* st4 = reinterpret_cast<float4*>(st);
 #pragma unroll
-                                    for (int k = 0; k < kSubCols / 4; k++)
-                                        if ((unsigned)(k - g0) <= gspan)
-                                            st4[k - g0] = make_float4(v[4 * k], v[4 * k + 1],
-                                                                      v[4 * k + 2], v[4 * k + 3]);
-                                    const float* sk = st + (k0 - 4 * g0);
-                                    float tv[NW];
+                            for (int k = 0; k < kSubCols / 4; k++)
+                                if ((unsigned)(k - g0) <= gspan)
+                                    st4[k - g0] = make_float4(v[4 * k], v[4 * k + 1],
+                                                              v[4 * k + 2], v[4 * k + 3]);
+                            const float* sk = st + (k0 - 4 * g0);
+                            float tv[NW];
 #pragma unroll
-                                    for (int i = 0; i < NW; i++)
-                                        tv[i] = ((unsigned)(i - lo) <= span) ? sk[i] : 0.0f;
-                                    float* wcol = win + (y - by);
+                            for (int q = 0; q < NW; q++)
+                                tv[q] = ((unsigned)(q - lo) <= span) ? sk[q] : 0.0f;
+                            float* wcol = win + (y - by);
 #pragma unroll
-                                    for (int i = 0; i < NW; i++)
-                                        if ((unsigned)(i - lo) <= span) wcol[i * 8] = g.alpha * tv[i];
-                                }
-                            }
+                            for (int q = 0; q < NW; q++)
+                                if ((unsigned)(q - lo) <= span) wcol[q * 8] = g.alpha * tv[q];
+                        }
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(bar(kBarTEmpty + a));
+                    w_b += DC_PROF_NOW() - t1;
+                }
+                if (!alive) break;
+                const long long t2 = DC_PROF_NOW();
+                quarter_sync(quarter);  // all passes have written this level's windows
+                if (pv) {
+                    bool vy[NW];
+#pragma unroll
+                    for (int k = 0; k < NW; k++)
+                        vy[k] = any && (unsigned)(by + k) < (unsigned)Hl;
+                    const float ux = 1.0f - dx, uy = 1.0f - dy;
+                    float* ol = out_e + (size_t)(l * D * D) * hw + p;
+                    // the quarter's warps split the output columns a (2, 2, 2, 1 at R = 3)
+                    constexpr int AW = (D + kSubWarps - 1) / kSubWarps;
+                    const int a0 = sub * AW;
+                    // taps of columns a0 .. a0 + AW, premultiplied by the x weights;
+                    // taps outside the level read as +0, which leaves every fmaf
+                    // below unchanged, as skipping them does in the reference
+                    float pu[AW + 1][NW], pd[AW + 1][NW];
+#pragma unroll
+                    for (int ii = 0; ii <= AW; ii++) {
+                        const int ix = a0 + ii;
+                        const bool vx = ix < NW && (unsigned)(bx + ix) < (unsigned)Wl;
+#pragma unroll
+                        for (int j = 0; j < NW; j++) {
+                            const float tt = (vx && vy[j]) ? win[ix * 8 + j] : 0.0f;
+                            pu[ii][j] = tt * ux;
+                            pd[ii][j] = tt * dx;
+                        }
+                    }
+#pragma unroll
+                    for (int ai = 0; ai < AW; ai++) {
+                        const int aa = a0 + ai;
+                        if (aa >= D) break;
+#pragma unroll
+                        for (int b = 0; b < D; b++) {
+                            // reference order: taps (a,b), (a,b+1), (a+1,b), (a+1,b+1)
+                            float acc = fmaf(pu[ai][b], uy, 0.0f);
+                            acc = fmaf(pu[ai][b + 1], dy, acc);
+                            acc = fmaf(pd[ai + 1][b], uy, acc);
+                            acc = fmaf(pd[ai + 1][b + 1], dy, acc);
+                            __stcs(ol + (size_t)(aa * D + b) * hw, acc);
                         }
                     }
                 }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(bar(kBarTEmpty + a));
-                w_b += DC_PROF_NOW() - t1;
+                quarter_sync(quarter);  // all are done reading before the next level
+                w_c += DC_PROF_NOW() - t2;
             }
-            if (!alive) break;
-            const long long t2 = DC_PROF_NOW();
-            quarter_sync(quarter);  // all slices have written this level's windows
-            if (pv) {
-                bool vy[NW];
-#pragma unroll
-                for (int k = 0; k < NW; k++) vy[k] = (unsigned)(by + k) < (unsigned)Hl;
-                const float ux = 1.0f - dx, uy = 1.0f - dy;
-                float* ol = out_e + (size_t)(l * D * D) * hw + p;
-                // the quarter's warps split the output columns a: 2, 2, 2, 1 (R = 3)
-                constexpr int AW = (D + kSubWarps - 1) / kSubWarps;  // columns per warp
-                const int a0 = sub * AW;
-                // taps of columns a0 .. a0 + AW (registers indexed statically);
-                // taps outside the level read as +0, which leaves every fmaf
-                // below unchanged, as skipping them does in the reference
-                float pu[AW + 1][NW], pd[AW + 1][NW];  // s * (1 - dx), s * dx
-#pragma unroll
-                for (int ii = 0; ii <= AW; ii++) {
-                    const int i = a0 + ii;
-                    const bool vx = i < NW && (unsigned)(bx + i) < (unsigned)Wl;
-#pragma unroll
-                    for (int j = 0; j < NW; j++) {
-                        const float t = (vx && vy[j]) ? win[i * 8 + j] : 0.0f;
-                        pu[ii][j] = t * ux;
-                        pd[ii][j] = t * dx;
-                    }
-                }
-#pragma unroll
-                for (int ai = 0; ai < AW; ai++) {
-                    const int a = a0 + ai;
-                    if (a >= D) break;
-#pragma unroll
-                    for (int b = 0; b < D; b++) {
-                        // reference order: taps (a,b), (a,b+1), (a+1,b), (a+1,b+1)
-                        float acc = fmaf(pu[ai][b], uy, 0.0f);
-                        acc = fmaf(pu[ai][b + 1], dy, acc);
-                        acc = fmaf(pd[ai + 1][b], uy, acc);
-                        acc = fmaf(pd[ai + 1][b + 1], dy, acc);
-                        __stcs(ol + (size_t)(a * D + b) * hw, acc);
-                    }
-                }
-            }
-            quarter_sync(quarter);  // all are done reading before the next level
-            w_c += DC_PROF_NOW() - t2;
+            (void)cend;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(kBarSEmpty + tb));
         }
-        if (lane == 0 && (warp == 2 || warp == 6)) {
-            DC_PROF_STORE(warp == 2 ? 5 : 10, w_a);
-            DC_PROF_STORE(warp == 2 ? 6 : 11, w_b);
-            DC_PROF_STORE(warp == 2 ? 7 : 12, w_c);
+        if (lane == 0 && warp == 2) {
+            DC_PROF_STORE(5, w_a);
+            DC_PROF_STORE(6, w_b);
+            DC_PROF_STORE(7, w_c);
         }
     }
 
@@ -599,7 +671,9 @@ int dc_launch_tc(dc_ctx* ctx, const int* ii, const int* jj, int M, const float* 
     P.ab_fmt = ctx->cfg.precision == DC_PREC_BF16 ? 1u : 0u;
     const Layout Ly = make_layout(P.atoms);
     const size_t smem = Ly.total + 1024;
-    dim3 grid((ctx->hw + kTileM - 1) / kTileM, M);
+    P.M = M;
+    const int ntiles = (ctx->hw + kTileM - 1) / kTileM * M;
+    dim3 grid(ntiles < ctx->num_sms ? ntiles : ctx->num_sms);
     const CUtensorMap* ta = reinterpret_cast<const CUtensorMap*>(ctx->tmap_a);
 #define DC_TC_LAUNCH(RR)                                                                   \
     do {                                                                                   \
