@@ -27,43 +27,57 @@ __global__ void __launch_bounds__(256) store_pack_kernel(const Tin* __restrict__
                                                           T* __restrict__ store, dc::Geom g,
                                                           int first, bool tf32) {
     extern __shared__ float sm[];
-    const int C = g.C;
+    // one CTA: one 8x8 tile of one slot, 32 of the C channels
+    constexpr int C = 32, lc = 5;
+    const int CT = g.C;  // channels of a store row
+    const int ngrp = CT / C;
+    const int grp = blockIdx.z % ngrp;
     // per-channel rows padded by one float so that the channel-strided reads of
     // the pixel-major write-out hit distinct banks
     float* t0 = sm;             // [C][65]  level 0, tile-local (ty*8+tx)
     float* t1 = t0 + C * 65;    // [C][17]  level 1
     float* t2 = t1 + C * 17;    // [C][5]   level 2
     float* t3 = t2 + C * 5;     // [C][1]   level 3
-    const int slot_local = blockIdx.z;
+    const int slot_local = blockIdx.z / ngrp;
     const int slot = first + slot_local;
     const int x0 = blockIdx.x * 8, y0 = blockIdx.y * 8;
-    const Tin* f = fmaps + (size_t)slot_local * C * g.hw;
-    T* st = store + (size_t)slot * g.frame_rows * C;
+    const Tin* f = fmaps + ((size_t)slot_local * CT + grp * C) * g.hw;
+    T* st = store + (size_t)slot * g.frame_rows * CT + grp * C;
 
-    for (int idx = threadIdx.x; idx < C * 64; idx += blockDim.x) {
-        int c = idx >> 6, k = idx & 63;
-        int y = y0 + (k >> 3), x = x0 + (k & 7);
-        float v = 0.0f;
-        if (y < g.h && x < g.w) v = dc::to_f32(f[(size_t)c * g.hw + y * g.w + x]);
-        t0[c * 65 + k] = v;
+    // all loads of a thread in flight at once (8 per thread)
+    static_assert(C * 64 % 256 == 0, "256 threads");
+    float lv[C * 64 / 256];
+#pragma unroll
+    for (int it = 0; it < C * 64 / 256; it++) {
+        const int idx = threadIdx.x + 256 * it;
+        const int c = idx >> 6, k = idx & 63;
+        const int y = y0 + (k >> 3), x = x0 + (k & 7);
+        lv[it] = (y < g.h && x < g.w) ? dc::to_f32(f[(size_t)c * g.hw + y * g.w + x]) : 0.0f;
+    }
+#pragma unroll
+    for (int it = 0; it < C * 64 / 256; it++) {
+        const int idx = threadIdx.x + 256 * it;
+        t0[(idx >> 6) * 65 + (idx & 63)] = lv[it];
     }
     __syncthreads();
     // level 0 rows
-    for (int idx = threadIdx.x; idx < C * 64; idx += blockDim.x) {
-        int k = idx / C, c = idx % C;
+#pragma unroll
+    for (int idx = threadIdx.x; idx < C * 64; idx += 256) {
+        int k = idx >> lc, c = idx & (C - 1);
         int y = y0 + (k >> 3), x = x0 + (k & 7);
         if (y < g.h && x < g.w)
-            st[(g.row0[0] + y * g.w + x) * C + c] = pack_value<T>(t0[c * 65 + k], tf32);
+            st[(g.row0[0] + y * g.w + x) * CT + c] = pack_value<T>(t0[c * 65 + k], tf32);
     }
     // cascaded pooling inside the tile: level l has (8 >> l)^2 tile-local cells
     float* src = t0;
     float* dstv[3] = {t1, t2, t3};
     for (int l = 1; l < g.levels; l++) {
         const int sw = 8 >> (l - 1), dw = 8 >> l;  // tile-local widths
+        const int ld = 3 - l;                        // log2(dw)
         float* dst = dstv[l - 1];
         for (int idx = threadIdx.x; idx < C * dw * dw; idx += blockDim.x) {
-            int c = idx / (dw * dw), k = idx % (dw * dw);
-            int ly = k / dw, lx = k % dw;
+            int c = idx >> (2 * ld), k = idx & (dw * dw - 1);
+            int ly = k >> ld, lx = k & (dw - 1);
             const float* s = src + c * (sw * sw + (sw > 1));
             float v = s[(2 * ly) * sw + 2 * lx] + s[(2 * ly) * sw + 2 * lx + 1];
             v = v + s[(2 * ly + 1) * sw + 2 * lx];
@@ -73,10 +87,10 @@ __global__ void __launch_bounds__(256) store_pack_kernel(const Tin* __restrict__
         __syncthreads();
         const int gy0 = y0 >> l, gx0 = x0 >> l;
         for (int idx = threadIdx.x; idx < C * dw * dw; idx += blockDim.x) {
-            int k = idx / C, c = idx % C;
-            int y = gy0 + k / dw, x = gx0 + k % dw;
+            int k = idx >> lc, c = idx & (C - 1);
+            int y = gy0 + (k >> ld), x = gx0 + (k & (dw - 1));
             if (y < g.H[l] && x < g.W[l])
-                st[(g.row0[l] + y * g.W[l] + x) * C + c] = pack_value<T>(dst[c * (dw * dw + (dw > 1)) + k], tf32);
+                st[(g.row0[l] + y * g.W[l] + x) * CT + c] = pack_value<T>(dst[c * (dw * dw + (dw > 1)) + k], tf32);
         }
         src = dst;
     }
@@ -85,8 +99,8 @@ __global__ void __launch_bounds__(256) store_pack_kernel(const Tin* __restrict__
 template <typename Tin, typename T>
 int launch_store_t(dc_ctx* ctx, const void* fmaps, int first, int count, cudaStream_t s) {
     dc::Geom g = dc::geom_of(ctx);
-    dim3 grid((g.w + 7) / 8, (g.h + 7) / 8, count);
-    size_t smem = (size_t)g.C * (65 + 17 + 5 + 1) * sizeof(float);
+    dim3 grid((g.w + 7) / 8, (g.h + 7) / 8, count * (g.C / 32));
+    size_t smem = (size_t)32 * (65 + 17 + 5 + 1) * sizeof(float);
     auto k = store_pack_kernel<Tin, T>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     k<<<grid, 256, smem, s>>>((const Tin*)fmaps, (T*)ctx->store, g, first,

@@ -118,7 +118,7 @@ __host__ __device__ constexpr Layout make_layout(int atoms) {
     L.stage_b = atoms * kChunkN * kRowBytes;
     L.win = L.b + kStagesB * L.stage_b;
     L.st = L.win + kTileM * kWinStride * 4;
-    L.sched = L.st + kEpiWarps * 32 * kStStride * 4;       // [2][levels] LevelSched
+    L.sched = L.st;                                          // [2][levels] LevelSched
     L.tinfo = L.sched + 2 * DC_MAX_LEVELS * sizeof(LevelSched);
     L.coords = L.tinfo + 2 * sizeof(TileInfo);              // [2][2][128] floats
     L.bars = L.coords + 2 * 2 * kTileM * 4;
@@ -199,7 +199,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t sA = smem_addr(base + Ly.a);
     const uint32_t sB = smem_addr(base + Ly.b);
     float* win_base = reinterpret_cast<float*>(base + Ly.win);
-    float* st_base = reinterpret_cast<float*>(base + Ly.st);
     LevelSched* sched_base = reinterpret_cast<LevelSched*>(base + Ly.sched);
     TileInfo* tinfo = reinterpret_cast<TileInfo*>(base + Ly.tinfo);
     float* scoords = reinterpret_cast<float*>(base + Ly.coords);
@@ -435,7 +434,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int sub = (warp - 2) >> 2;    // which columns of a chunk (0..kSubWarps-1)
         const int ti_px = 32 * quarter + lane;
         float* win = win_base + ti_px * kWinStride;
-        float* st = st_base + ((warp - 2) * 32 + lane) * kStStride;
         const uint32_t tl = tmem + ((uint32_t)(32 * quarter) << 16);
         const int cwarp = kSubCols * kPasses * sub;  // first chunk column of this warp
         int gc = 0, i = 0;
@@ -495,10 +493,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const int ya = max(ylo, ch.y0 + rlo);
                         const int yb = min(yhi, ch.y0 + rhi);
                         const int xa = max(xlo, ch.x0), xb = min(xhi, ch.x0 + ch.seg - 1);
-                        const bool need = any && ya <= yb && xa <= xb;
+                        bool need = any && ya <= yb && xa <= xb;
+#if defined(DC_TC_EXP) && DC_TC_EXP == 2
+                        need = false;
+#endif
                         if (!__any_sync(0xffffffffu, need)) continue;
                         float v[kSubCols];
                         tmem_ld32(tl + (uint32_t)(a * kChunkN + cb), v);
+#if defined(DC_TC_EXP) && DC_TC_EXP == 1
+                        if (v[5] != 1234.5f) continue;
+#endif
                         if (!need) continue;
                         const int kofs = -ch.x0 - cb;
                         const int ia = xa - bx, ib = xb - bx;  // valid tap range
@@ -507,25 +511,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                             const int lo = max(ia, -k0), hi = min(ib, kSubCols - 1 - k0);
                             if (lo > hi) continue;
                             const unsigned span = (unsigned)(hi - lo);
-                            // stage the <= 3 16-byte groups holding this row's taps,
-                            // compacted: group g goes to slot g - g0
-                            const int g0 = (k0 + lo) >> 2;
-                            const unsigned gspan = (unsigned)(((k0 + hi) >> 2) - g0);
-                            float4* st4 = reinterpret_cast<float4*>(st);
-#pragma unroll
-                            for (int k = 0; k < kSubCols / 4; k++)
-                                if ((unsigned)(k - g0) <= gspan)
-                                    st4[k - g0] = make_float4(v[4 * k], v[4 * k + 1],
-                                                              v[4 * k + 2], v[4 * k + 3]);
-                            const float* sk = st + (k0 - 4 * g0);
-                            float tv[NW];
-#pragma unroll
-                            for (int q = 0; q < NW; q++)
-                                tv[q] = ((unsigned)(q - lo) <= span) ? sk[q] : 0.0f;
+                            // tap q sits at column k0 + q; the tap whose column is
+                            // congruent to r mod 8 is in register 8 * (column >> 3) + r,
+                            // so each of the 8 residues needs only a 4-way select
                             float* wcol = win + (y - by);
 #pragma unroll
-                            for (int q = 0; q < NW; q++)
-                                if ((unsigned)(q - lo) <= span) wcol[q * 8] = g.alpha * tv[q];
+                            for (int r = 0; r < 8; r++) {
+                                const int q = (r - k0) & 7;
+                                const int kk = (k0 + q) >> 3;
+                                const float val = (kk & 2) ? ((kk & 1) ? v[24 + r] : v[16 + r])
+                                                           : ((kk & 1) ? v[8 + r] : v[r]);
+                                if ((unsigned)(q - lo) <= span) wcol[q * 8] = g.alpha * val;
+                            }
                         }
                     }
                     tc_fence_before();
