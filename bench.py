@@ -48,6 +48,9 @@ def parse():
     ap.add_argument("--precision", default="fp16", choices=["fp32", "tf32", "bf16", "fp16"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-gpu", action="store_true")
+    ap.add_argument("--materialise", action="store_true",
+                    help="store the volume pyramid (dc_build_volume) and look up from it, "
+                         "the reference's own data flow, instead of the fused path")
     return ap.parse_args()
 
 
@@ -226,11 +229,21 @@ def main():
     flush_sink = torch.empty((), dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream()
 
+    vols = ([torch.empty(sh, dtype=torch.float32, device=dev) for sh in dc.volume_shapes(M)]
+            if args.materialise else None)
+
+    def corr():
+        if vols is not None:
+            dc.build_volume(ii_d, jj_d, vols)
+            dc.lookup(vols, coords, out)
+        else:
+            dc.build_and_lookup(ii_d, jj_d, coords, out)
+
     def step():
         if pg is not None:
             replicate_frames(fm)
         dc.set_frames(fm)
-        dc.build_and_lookup(ii_d, jj_d, coords, out)
+        corr()
 
     for _ in range(max(args.warmup, 3)):
         step()
@@ -258,7 +271,7 @@ def main():
             replicate_frames(fm)
         dc.set_frames(fm)
         ev[s][2].record(stream)
-        dc.build_and_lookup(ii_d, jj_d, coords, out)
+        corr()
         ev[s][3].record(stream)
         ev[s][1].record(stream)
     torch.cuda.synchronize()

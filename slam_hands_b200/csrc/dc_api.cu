@@ -162,7 +162,8 @@ int dc_build_volume(dc_ctx* ctx, const int* ii, const int* jj, int M, float* con
     if (rc) return rc;
     if (!vols || !vols[0]) return dc_fail(ctx, DC_ERR_INVALID_ARG, "vols[0] is NULL");
     if (M == 0) return DC_OK;
-    rc = dc_launch_volume_ffma(ctx, ii, jj, M, vols[0], (cudaStream_t)stream);
+    rc = ctx->tc_ready ? dc_launch_volume_tc(ctx, ii, jj, M, vols[0], (cudaStream_t)stream)
+                       : dc_launch_volume_ffma(ctx, ii, jj, M, vols[0], (cudaStream_t)stream);
     if (rc) return rc;
     return dc_launch_volume_pyramid(ctx, vols, M, (cudaStream_t)stream);
 }

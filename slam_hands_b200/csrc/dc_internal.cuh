@@ -120,6 +120,8 @@ int dc_launch_store(dc_ctx* ctx, const void* fmaps, int dtype, int first, int co
                     cudaStream_t s);
 int dc_launch_volume_ffma(dc_ctx* ctx, const int* ii, const int* jj, int M, float* vol0,
                           cudaStream_t s);
+int dc_launch_volume_tc(dc_ctx* ctx, const int* ii, const int* jj, int M, float* vol0,
+                        cudaStream_t s);
 int dc_launch_volume_pyramid(dc_ctx* ctx, float* const* vols, int M, cudaStream_t s);
 int dc_launch_pool2x2(const float* in, float* out, long long N, int H, int W,
                       cudaStream_t s);
