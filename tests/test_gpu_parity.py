@@ -280,3 +280,35 @@ def test_full_path_vs_reference_fp16(cuda, oracle):
     err = normwise(out, ref_out)
     print(f"fused fp16 vs reference: normwise {err:.3e} maxabs {np.abs(out - ref_out).max():.3e}")
     assert err < TOL_LOW
+
+
+# ---------------------------------------------------------------- drop-in methods
+
+@pytest.mark.parametrize("precision", ["fp32", "fp16"])
+def test_cudadroid_method_names(cuda, oracle, precision):
+    # build_correlation / sample_correlation / batch_build_and_sample_correlation
+    # with the reference's arguments (main.cu:1500, :1529, :1555)
+    h, w = 24, 32
+    rng = np.random.default_rng(31)
+    K = 4
+    fm = rng.standard_normal((K, 128, h, w), dtype=np.float32)
+    dc = DroidCorrelation(h, w, precision=precision, max_frames=K, max_edges=4)
+    dc.set_frames(torch.from_numpy(fm).cuda())
+    # single edge: volumes then the corr_index_kernel arithmetic
+    dc.build_correlation(2, 1)
+    coords = (configs.grid_coords(h, w)[None] + rng.normal(0, 2, (1, 2, h, w))).astype(np.float32)
+    out1 = torch.empty(196, h, w, device="cuda")
+    dc.sample_correlation(torch.from_numpy(coords[0]).cuda(), out1)
+    fi, fj = round_like(fm[2], precision), round_like(fm[1], precision)
+    V = oracle.volume_f64(fi, fj, 1 / 16)
+    ref1 = oracle.lookup(oracle.pyramid(V[None], h, w, 4), coords, h, w, 3, oracle.LOOKUP_SINGLE)[0]
+    assert normwise(out1.cpu().numpy(), ref1) < 1e-5
+    assert dc.corr_volume.shape == (h * w, h * w)
+    # batch: edges from the host lists, as DroidState::ii_host / jj_host
+    dc.ii_host = [0, 1, 2, 3, 0]
+    dc.jj_host = [1, 2, 3, 0, 2]
+    c4 = (configs.grid_coords(h, w)[None] + rng.normal(0, 2, (3, 2, h, w))).astype(np.float32)
+    out = torch.empty(3, 196, h, w, device="cuda")
+    dc.batch_build_and_sample_correlation(3, 1, torch.from_numpy(c4).cuda(), out)
+    exp = oracle_alt(oracle, fm, np.array([1, 2, 3]), np.array([2, 3, 0]), c4, 1 / 16, precision)
+    assert normwise(out.cpu().numpy(), exp) < 1e-4
