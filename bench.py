@@ -13,8 +13,9 @@ reference's own: FP16 fmaps, fp32 accumulate).
 --impl reference times the reference's CPU path (the C/OpenMP restatement in
 oracle/, the reference having no CPU implementation of its own) on the host
 cores.  Under torchrun (N>1) each rank owns a distinct seeded batch of 48
-edges (weak scaling) and the step starts with an NCCL broadcast of the step's
-feature maps from rank 0.
+edges (weak scaling; the backend workloads C3/C5 split one edge list instead)
+and every step starts with rank 0 packing the step's keyframes and one NCCL
+broadcast of the packed store to the other ranks.
 """
 from __future__ import annotations
 
@@ -189,7 +190,7 @@ def main():
         return run_reference_arm(args, wl)
 
     from slam_hands_b200 import DroidCorrelation
-    from slam_hands_b200.shard import edge_range, replicate_frames
+    from slam_hands_b200.shard import edge_range, replicate_store
 
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
@@ -240,9 +241,11 @@ def main():
             dc.build_and_lookup(ii_d, jj_d, coords, out)
 
     def step():
+        # rank 0 packs the step's keyframes and broadcasts the packed slots
+        if rank == 0:
+            dc.set_frames(fm)
         if pg is not None:
-            replicate_frames(fm)
-        dc.set_frames(fm)
+            replicate_store(dc, 0, wl.frames)
         corr()
 
     for _ in range(max(args.warmup, 3)):
@@ -267,9 +270,10 @@ def main():
     for s in range(args.steps):
         torch.sum(flush, dim=0, out=flush_sink)
         ev[s][0].record(stream)
+        if rank == 0:
+            dc.set_frames(fm)
         if pg is not None:
-            replicate_frames(fm)
-        dc.set_frames(fm)
+            replicate_store(dc, 0, wl.frames)
         ev[s][2].record(stream)
         corr()
         ev[s][3].record(stream)
@@ -299,13 +303,15 @@ def main():
     jj_d2 = torch.empty_like(jj_d)
 
     def e2e_step():
-        fm_d2.copy_(fm_h, non_blocking=True)
+        if rank == 0:  # the other ranks receive the packed store by broadcast
+            fm_d2.copy_(fm_h, non_blocking=True)
         coords_d2.copy_(coords_h, non_blocking=True)
         ii_d2.copy_(ii_h, non_blocking=True)
         jj_d2.copy_(jj_h, non_blocking=True)
+        if rank == 0:
+            dc.set_frames(fm_d2)
         if pg is not None:
-            replicate_frames(fm_d2)
-        dc.set_frames(fm_d2)
+            replicate_store(dc, 0, wl.frames)
         dc.build_and_lookup(ii_d2, jj_d2, coords_d2, out)
         out_h.copy_(out, non_blocking=True)
 
@@ -327,7 +333,7 @@ def main():
         t = torch.tensor([e2e_ms], device=dev)
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
         e2e_ms = t.item()
-    h2d = fm_h.numel() * 4 + coords_h.numel() * 4 + 2 * M * 4
+    h2d = fm_h.numel() * 4 + coords_h.numel() * 4 + 2 * M * 4  # rank 0 (others: no frames)
     d2h = out_h.numel() * 4
 
     # ---- parity spot check of the timed output (cheap, rank 0)

@@ -110,6 +110,13 @@ long long dc_context_bytes(const dc_ctx* ctx);
 int dc_set_frames(dc_ctx* ctx, const void* fmaps_dev, int dtype, int first_slot, int count,
                   dc_stream_t stream);
 
+/* Device address and byte size of store slots first_slot .. first_slot+count-1
+ * (contiguous).  For replicating packed keyframes to other GPUs (e.g. one NCCL
+ * broadcast of the packed slots instead of re-packing on every GPU).  No
+ * reference counterpart: the reference runs on one GPU. */
+int dc_store_slots(dc_ctx* ctx, int first_slot, int count, void** ptr_out,
+                   long long* bytes_out);
+
 /* Materialised volumes for M edges (CudaDroid::build_correlation, main.cu:1500,
  * and steps 1-3 of batch_build_and_sample_correlation, main.cu:1558-1596):
  * vol0 = alpha * f_ii^T f_jj, then vol_l = 2x2 average of vol_{l-1} over the

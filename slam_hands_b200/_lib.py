@@ -62,6 +62,7 @@ SIGNATURES = {
     "dc_alt_lookup": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp]),
     "dc_launch_count": (_ll, [_vp]),
     "dc_device_status": (_i, [_vp, _vp]),
+    "dc_store_slots": (_i, [_vp, _i, _i, ctypes.POINTER(_vp), ctypes.POINTER(_ll)]),
     "dc_build_and_lookup_static": (_i, [ctypes.POINTER(DcConfig), _vp, _i, _i, _vp, _vp, _i,
                                         _vp, _vp, _vp]),
 }

@@ -120,6 +120,19 @@ class DroidCorrelation:
         self._check(self.lib.dc_set_frames(self._ctx, fmaps.data_ptr(), dt, first_slot,
                                            fmaps.shape[0], _stream(stream)))
 
+    def store_slots(self, first_slot: int, count: int) -> torch.Tensor:
+        """uint8 view [bytes] of the packed store slots first_slot..+count (device
+        memory owned by the library; valid while this object lives)."""
+        ptr, nbytes = ctypes.c_void_p(), ctypes.c_longlong()
+        self._check(self.lib.dc_store_slots(self._ctx, first_slot, count, ctypes.byref(ptr),
+                                            ctypes.byref(nbytes)))
+
+        class _View:
+            __cuda_array_interface__ = {"shape": (nbytes.value,), "typestr": "|u1",
+                                        "data": (ptr.value, False), "version": 3}
+
+        return torch.as_tensor(_View(), device=self.device)
+
     # -- tensor-level calls ----------------------------------------------------
     def volume_shapes(self, M: int):
         return [(M, self.hw, self.h >> l, self.w >> l) for l in range(self.levels)]

@@ -155,6 +155,16 @@ int dc_set_frames(dc_ctx* ctx, const void* fmaps, int dtype, int first, int coun
     return dc_launch_store(ctx, fmaps, dtype, first, count, (cudaStream_t)stream);
 }
 
+int dc_store_slots(dc_ctx* ctx, int first, int count, void** ptr, long long* bytes) {
+    if (!ctx || !ptr || !bytes) return DC_ERR_INVALID_ARG;
+    if (first < 0 || count < 0 || first + count > ctx->cfg.max_frames)
+        return dc_fail(ctx, DC_ERR_INVALID_ARG, "slot range outside [0, max_frames)");
+    const long long slot_bytes = ctx->frame_rows * ctx->cfg.channels * ctx->elem_bytes;
+    *ptr = static_cast<char*>(ctx->store) + first * slot_bytes;
+    *bytes = count * slot_bytes;
+    return DC_OK;
+}
+
 int dc_build_volume(dc_ctx* ctx, const int* ii, const int* jj, int M, float* const* vols,
                     dc_stream_t stream) {
     if (!ctx) return DC_ERR_INVALID_ARG;

@@ -25,3 +25,12 @@ def replicate_frames(fmaps, src: int = 0, group=None) -> None:
     import torch.distributed as dist
 
     dist.broadcast(fmaps, src=src, group=group)
+
+
+def replicate_store(dc, first_slot: int, count: int, src: int = 0, group=None) -> None:
+    """Broadcast packed store slots from rank `src` (after its set_frames), so the
+    other ranks skip packing: the packed fp16 pyramid is smaller than the fp32
+    maps and identical on every rank."""
+    import torch.distributed as dist
+
+    dist.broadcast(dc.store_slots(first_slot, count), src=src, group=group)

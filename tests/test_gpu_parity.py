@@ -312,3 +312,26 @@ def test_cudadroid_method_names(cuda, oracle, precision):
     dc.batch_build_and_sample_correlation(3, 1, torch.from_numpy(c4).cuda(), out)
     exp = oracle_alt(oracle, fm, np.array([1, 2, 3]), np.array([2, 3, 0]), c4, 1 / 16, precision)
     assert normwise(out.cpu().numpy(), exp) < 1e-4
+
+
+def test_store_slots_copy_equals_local_pack(cuda):
+    # a second context that receives the packed slots by copy (what the NCCL
+    # broadcast of shard.replicate_store does between GPUs) computes bit-identical
+    # results to the context that packed them
+    h, w = 24, 32
+    dc, fm, ii, jj, coords = setup(h, w, K=3, M=3, precision="fp16", max_edges=4)
+    other = DroidCorrelation(h, w, precision="fp16", alpha=1 / 16, max_frames=4, max_edges=4)
+    src = dc.store_slots(0, 3)
+    dst = other.store_slots(0, 3)
+    assert src.numel() == dst.numel() > 0 and src.dtype == torch.uint8
+    dst.copy_(src)
+    ii_d = torch.from_numpy(ii).cuda()
+    jj_d = torch.from_numpy(jj).cuda()
+    c = torch.from_numpy(coords).cuda()
+    a = torch.empty(3, 196, h, w, device="cuda")
+    b = torch.empty_like(a)
+    dc.build_and_lookup(ii_d, jj_d, c, a)
+    other.build_and_lookup(ii_d, jj_d, c, b)
+    assert torch.equal(a, b)
+    with pytest.raises(DroidCorrError):
+        dc.store_slots(2, 3)
