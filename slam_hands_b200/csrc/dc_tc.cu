@@ -425,6 +425,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             DC_PROF_STORE(2, w_a);
             DC_PROF_STORE(3, w_b);
+            DC_PROF_STORE(8, gc);
+            DC_PROF_STORE(9, i);
         }
         __syncwarp();
     } else {

@@ -2,9 +2,16 @@
 
 Edges are independent, so the path shards with no data-path collective: rank r
 owns a contiguous, near-equal range of the edge list and writes its outputs
-locally.  The only exchange is the replication of keyframe feature maps, one
-NCCL broadcast from rank 0 (the reference runs on one GPU and has no
-counterpart; cuda_slam/main.cu:1555-1613 processes every edge itself).
+locally.  The only exchange is the replication of keyframes, one NCCL
+broadcast from rank 0: either of the raw feature maps (`replicate_frames`) or of
+the packed store slots (`replicate_store`).  The reference runs on one GPU and
+has no counterpart (cuda_slam/main.cu:1555-1613 processes every edge itself).
+
+Failure detection is on the host, between steps: every rank posts a heartbeat
+for the step to the rendezvous store before it launches the step's collective,
+and `peers_alive` tells the others, within a deadline, which ranks did not, so
+that no rank enters a broadcast a dead peer will never join.  A collective that
+is entered anyway ends with an error after `timeout_s` (`replicate_frames`).
 """
 from __future__ import annotations
 
@@ -20,11 +27,38 @@ def edge_range(num_edges: int, world: int, rank: int) -> Tuple[int, int]:
     return start, start + base + (1 if rank < extra else 0)
 
 
-def replicate_frames(fmaps, src: int = 0, group=None) -> None:
-    """Broadcast keyframe feature maps [K, C, h, w] from rank `src` in place."""
+def replicate_frames(fmaps, src: int = 0, group=None, timeout_s: float = None) -> None:
+    """Broadcast keyframe feature maps [K, C, h, w] from rank `src` in place.
+    With `timeout_s`, a peer that never joins makes this raise RuntimeError after
+    that many seconds instead of blocking."""
+    import datetime
+
     import torch.distributed as dist
 
-    dist.broadcast(fmaps, src=src, group=group)
+    if timeout_s is None:
+        dist.broadcast(fmaps, src=src, group=group)
+        return
+    work = dist.broadcast(fmaps, src=src, group=group, async_op=True)
+    work.wait(timeout=datetime.timedelta(seconds=timeout_s))
+
+
+def peers_alive(store, step: int, world: int, rank: int, timeout_s: float = 1.0):
+    """Post this rank's heartbeat for `step` and wait up to `timeout_s` for the
+    other ranks' heartbeats.  Returns the sorted list of ranks that did not post
+    (empty when all are alive).  `store` is the rendezvous store
+    (torch.distributed TCPStore / FileStore)."""
+    import time
+
+    store.set(f"dc_alive/{step}/{rank}", "1")
+    keys = {r: f"dc_alive/{step}/{r}" for r in range(world) if r != rank}
+    deadline = time.monotonic() + timeout_s
+    missing = sorted(keys)
+    while missing:
+        missing = [r for r in missing if not store.check([keys[r]])]
+        if not missing or time.monotonic() >= deadline:
+            break
+        time.sleep(0.01)
+    return missing
 
 
 def replicate_store(dc, first_slot: int, count: int, src: int = 0, group=None) -> None:

@@ -61,3 +61,50 @@ def test_replication_and_sharding_gloo():
     ref = float(torch.from_numpy(configs.make_fmaps_np(configs.WORKLOADS["C2"], frames=3)).double().sum())
     assert all(abs(r[1] - ref) < 1e-6 * max(1.0, abs(ref)) for r in res)
     assert res[0][2] == 0 and res[0][3] == res[1][2] and res[1][3] == 2048
+
+
+def _failing_worker(rank, world, port, q):
+    # rank 1 fails before step 1 (raises on the host, joins nothing); rank 0
+    # learns of it from the missing heartbeat and skips the step's broadcast,
+    # and a broadcast entered anyway ends with an error after its deadline
+    from datetime import timedelta
+
+    from slam_hands_b200.shard import peers_alive, replicate_frames
+
+    store = dist.TCPStore("127.0.0.1", port, world, rank == 0, timeout=timedelta(seconds=30))
+    dist.init_process_group("gloo", store=store, rank=rank, world_size=world,
+                            timeout=timedelta(seconds=30))
+    fm = torch.ones(2, 4, 3, 5) * (rank + 1)
+    missing0 = peers_alive(store, 0, world, rank, timeout_s=10.0)
+    replicate_frames(fm)  # step 0: everyone alive
+    if rank == 1:
+        q.put((rank, missing0, None, None))
+        store.set("dc_test/rank1_done", "1")
+        return  # "fails": no heartbeat for step 1, never joins again
+    missing1 = peers_alive(store, 1, world, rank, timeout_s=1.0)
+    store.wait(["dc_test/rank1_done"])
+    try:
+        replicate_frames(fm, timeout_s=1.0)
+        raised = False
+    except RuntimeError:
+        raised = True
+    q.put((rank, missing0, missing1, raised))
+    q.close()
+    q.join_thread()  # flush the result before the hard exit
+    os._exit(0)  # the process group cannot be torn down with a dead peer
+
+
+def test_dead_rank_detected_on_host_gloo():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict((r[0], r) for r in (q.get(timeout=120) for _ in range(world)))
+    for p in procs:
+        p.join(timeout=60)
+    assert res[1][1] == [] and res[0][1] == []      # step 0: all heartbeats present
+    assert res[0][2] == [1]                          # step 1: rank 1 reported missing
+    assert res[0][3] is True                         # a broadcast entered anyway errors out
