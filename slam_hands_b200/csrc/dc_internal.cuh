@@ -37,6 +37,9 @@ struct dc_ctx {
     int* dev_err = nullptr;  // device error word raised by bounded device waits
     // tensor map of the store for the tensor-core kernel (CUtensorMap storage)
     alignas(64) unsigned char tmap_a[128];
+    // per level, a 4-D map [slot][H_l][W_l][C] of the same store with boxes of
+    // 4 target rows x 8 target columns x 64 channels (the fused kernel's B boxes)
+    alignas(64) unsigned char tmap_b[DC_MAX_LEVELS][128];
     bool tc_ready = false;
     std::string err;
 };

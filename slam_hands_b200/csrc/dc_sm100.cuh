@@ -51,17 +51,24 @@ __device__ __forceinline__ uint64_t globaltimer() {
 // Wait for phase `parity` of a barrier, giving up after `limit_ns` or when
 // *abort (if given) becomes non-zero.  Returns false on give-up (the caller records the
 // failure and leaves its loop); no wait in the library is unbounded.
+// mbarrier.try_wait itself suspends the thread for a hardware time window, so
+// the loop polls without sleeping (a sleep would add its whole length to every
+// hand-off between pipeline roles); only a wait already longer than 50 us backs
+// off with __nanosleep, and the abort flag and the clock are read every 64 polls.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
                                           const volatile int* abort,
                                           uint64_t limit_ns = 2000000000ull) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
+    bool slow = false;
     for (uint32_t it = 1;; it++) {
         if (mbar_try_wait(bar, parity)) return true;
-        __nanosleep(128);  // back off: spinning warps would take issue slots
-        if ((it & 255u) == 0) {
+        if (slow) __nanosleep(256);
+        if ((it & 63u) == 0) {
             if (abort && *abort) return false;
-            if (globaltimer() - t0 > limit_ns) return false;
+            const uint64_t dt = globaltimer() - t0;
+            if (dt > limit_ns) return false;
+            slow = dt > 50000ull;
         }
     }
 }
@@ -77,6 +84,16 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int 
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
         " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
         "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(bar)
+        : "memory");
+}
+
+// 4-D tiled load global -> shared (coordinates innermost first).
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, int c0, int c1,
+                                            int c2, int c3, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
         : "memory");
 }
 

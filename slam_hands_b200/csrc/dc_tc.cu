@@ -4,32 +4,42 @@
 // (cuda_slam/main.cu:1555-1613) that never writes a volume.  For one edge e and
 // one tile of 128 source pixels p, the lookup needs, per level l, the volume
 // values V_l[p][q] = alpha * <f_ii[:, p], P_l f_jj[:, q]> at the (2r+2)^2 taps
-// around each pixel's scaled coordinate.  The CTA
-//   1. reduces, over its 128 pixels, the range of target rows any window of
-//      level l touches (so only those rows of the level are correlated);
-//   2. streams those rows of the pooled target map P_l f_jj (pixel-major store,
-//      K-major operand) through shared memory with TMA in row-aligned chunks of
-//      at most 128 target pixels, double-buffered;
-//   3. computes each 128 x n x C correlation chunk with tcgen05.mma (kind::f16,
-//      fp16 or bf16 operands, fp32 accumulation in TMEM, four accumulators so the
-//      epilogue of chunk c overlaps the MMAs of the next chunks);
-//   4. reads back only the TMEM columns that hold some pixel's window taps
-//      (tcgen05.ld), stages the 16-byte groups a pixel needs in shared memory,
-//      picks its taps into its window, and after the last chunk of a level forms
-//      the (2r+1)^2 bilinear outputs in the reference's rounding order
-//      (main.cu:1196-1213), stored as coalesced 128-byte rows of
-//      out[e][l*(2r+1)^2 + a*(2r+1) + b][p].
+// around each pixel's scaled coordinate.  Per tile:
+//   1. a scheduler warp reduces, over the tile's 128 pixels, the range of target
+//      rows (and, for rows wider than 256 pixels, of row segments) any window of
+//      level l touches, one tile ahead of the others;
+//   2. the producer streams those rows of the pooled target map P_l f_jj
+//      (pixel-major store, K-major operand) into shared memory: one 4-D TMA box
+//      per 64-channel K atom holds `br` whole rows of `wbox` pixels (rows padded
+//      to a multiple of 8 pixels, out-of-image pixels read as zeros), at most 256
+//      targets -- few, large boxes, because a TMA box costs a fixed few hundred
+//      cycles whatever its size;
+//   3. one thread computes each 128 x N x C chunk with tcgen05.mma (kind::f16,
+//      fp16 or bf16 operands, fp32 accumulation in TMEM, two accumulators so the
+//      epilogue of one chunk overlaps the MMAs of the next);
+//   4. the epilogue reads the accumulator in 32-column loads (tcgen05.ld); each
+//      load is four 8-column strips, every strip 8 consecutive target pixels of
+//      one row starting at a multiple of 8.  A window of 8 columns starting at
+//      bx touches only strips bx/8 and bx/8 + 1, so a lane copies a strip it
+//      needs into slot 0 or 1 of its window row with two 16-byte stores -- no
+//      per-tap selection;
+//   5. after the last chunk of a level, forms the (2r+1)^2 bilinear outputs in
+//      the reference's order of accumulation (main.cu:1196-1213), reading window
+//      column x at slot column (bx mod 8) + x, and stores them as
+//      out[e][l*(2r+1)^2 + a*(2r+1) + b][p] (consecutive pixels per warp).
 //
-// Warp roles (320 threads): warp 0 issues TMA, warp 1 allocates TMEM and issues
-// MMAs (one elected lane each), warps 2..9 are the epilogue.  Warp w reads TMEM
-// lanes 32*(w%4) .. 32*(w%4)+31, i.e. tile pixels 32*(w%4) + lane; the two warps
-// of a lane quarter take the two 64-column halves of a chunk and split the
-// outputs.
+// Warp roles (608 threads): warp 0 issues TMA, warp 1 allocates TMEM and issues
+// MMAs (one elected lane each), warps 2..17 are the epilogue, warp 18 schedules
+// tiles.  Warp w reads TMEM lanes 32*(w%4) .. 32*(w%4)+31, i.e. tile pixels
+// 32*(w%4) + lane; the four warps of a lane quarter take a chunk's 32-column
+// loads round-robin and split the bilinear outputs by column.
 //
 // Every mbarrier wait is bounded (2 s); on a time-out the CTA raises the
 // context's device error word, stops all roles, waits (bounded) for its TMA
 // copies in flight, frees its TMEM and returns.  No TMA multicast is used.
 #include <cuda.h>
+
+#include <cstring>
 
 #include "dc_internal.cuh"
 #include "dc_sm100.cuh"
@@ -39,48 +49,60 @@ namespace {
 using namespace dc::sm100;
 
 constexpr int kTileM = 128;      // source pixels per CTA = MMA M = TMEM lanes
-constexpr int kChunkN = 256;     // max target pixels per chunk = MMA N
-constexpr int kSubCols = 32;     // chunk columns per epilogue warp
+constexpr int kChunkN = 256;     // max targets per chunk = MMA N
+constexpr int kStrip = 8;        // target pixels per strip
+constexpr int kLoadCols = 32;    // TMEM columns per epilogue load (4 strips)
 constexpr int kStagesB = 2;      // shared-memory stages of target rows
-constexpr int kAcc = 2;          // TMEM accumulators (kAcc * kChunkN = 512 columns)
+constexpr int kAcc = 2;          // TMEM accumulators
+constexpr int kAccCols = 256;    // TMEM columns per accumulator
 constexpr int kSubWarps = 4;     // epilogue warps per TMEM lane quarter
-constexpr int kPasses = kChunkN / (kSubWarps * 32);  // 32-column passes per warp and chunk
 constexpr int kEpiWarps = 4 * kSubWarps;
-constexpr int kThreads = 64 + 32 * kEpiWarps;
-constexpr int kWinStride = 65;   // floats per pixel window row (64 taps + pad)
-constexpr int kStStride = 12;   // floats per staging row: 3 16-byte groups (bank-conflict free)
-constexpr uint32_t kTmemCols = kAcc * kChunkN;
+constexpr int kSchedWarp = 2 + kEpiWarps;
+constexpr int kThreads = 32 * (kSchedWarp + 1);
+constexpr int kWinRow = 16;      // floats per window row: two 8-column strip slots
+constexpr int kWinStride = 8 * kWinRow;      // floats per pixel
+// Within a window row the four 16-byte units (slot 0 low/high, slot 1 low/high)
+// are stored at unit index u ^ (pixel & 3), which spreads neighbouring pixels'
+// stores and loads over the banks.
+constexpr uint32_t kTmemCols = kAcc * kAccCols;
 constexpr uint32_t kRowBytes = 128;  // one 128-byte K atom per operand row
+static_assert(kChunkN <= kAccCols && kChunkN % 16 == 0, "MMA N");
 
-// A chunk is `nrows` consecutive target rows of one level, each the segment
-// [x0, x0 + seg) of the row (seg = W when whole rows fit, else a row is split).
-struct ChunkDesc {
-    int n, row;            // MMA N (multiple of 16), store row of the first pixel
-    int y0, x0, seg, cols; // level coordinates of chunk column 0, segment, columns
+// Per-level constants of the target boxes (host-computed): a box holds br rows
+// of wbox pixels (wbox a multiple of 8, br * wbox <= 256); a row wider than
+// wbox is split into segs segments.
+struct LevelBox {
+    int wbox, br, segs;
+    float inv_wbox;
 };
 
-// Per-level chunk schedule of one tile: chunks first .. first+count-1 cover the
-// target rows ylo..yhi of the level, rows_per whole rows per chunk, or for rows
-// wider than a chunk, segs segments of seg_max pixels per row.
+// Per-level schedule of one tile: target rows ylo .. ylo + nrows - 1 and row
+// segments sg0 .. sg0 + nsg - 1; chunks first .. first + count - 1 of the tile.
+// With one segment per row a chunk holds br consecutive rows; otherwise a chunk
+// is one segment of one row.
 struct LevelSched {
-    int first, count, ylo, yhi, rows_per, seg_max, segs, W;
+    int first, count, ylo, nrows, sg0, nsg, pad0, pad1;
 };
 
-__device__ __forceinline__ ChunkDesc make_chunk(const LevelSched& L, int idx,
-                                                long long row_base) {
-    ChunkDesc c;
-    int r = idx, sg = 0;
-    if (L.segs > 1) {
-        r = idx / L.segs;
-        sg = idx - r * L.segs;
+struct ChunkGeo {
+    int y0, x0, rows, cols, n;  // first row and column, rows, real targets, MMA N
+};
+
+__device__ __forceinline__ ChunkGeo chunk_geo(const LevelSched& L, const LevelBox& B, int c) {
+    ChunkGeo g;
+    if (B.segs == 1) {
+        g.y0 = L.ylo + c * B.br;
+        g.x0 = 0;
+        g.rows = min(B.br, L.ylo + L.nrows - g.y0);
+    } else {
+        const int r = c / L.nsg;
+        g.y0 = L.ylo + r;
+        g.x0 = (L.sg0 + c - r * L.nsg) * B.wbox;
+        g.rows = 1;
     }
-    c.y0 = L.ylo + r * L.rows_per;
-    c.x0 = sg * L.seg_max;
-    c.seg = min(L.seg_max, L.W - c.x0);
-    c.cols = min(L.rows_per, L.yhi - c.y0 + 1) * c.seg;
-    c.n = (c.cols + 15) & ~15;
-    c.row = (int)(row_base + (long long)c.y0 * L.W + c.x0);
-    return c;
+    g.cols = g.rows * B.wbox;
+    g.n = (g.cols + 15) & ~15;
+    return g;
 }
 
 // floor(v / d) for 0 <= v < 2^12 and 1 <= d <= 2^12 from d's reciprocal: the
@@ -90,8 +112,16 @@ __device__ __forceinline__ int div_small(int v, float inv_d) {
     return (int)(((float)v + 0.5f) * inv_d);
 }
 
+// The operand tensor maps: A = the 2-D store (128 source pixels x 64 channels
+// boxes), B[l] = level l as [slot][H_l][W_l][C] (br x wbox x 64 boxes).
+struct TcMaps {
+    CUtensorMap a;
+    CUtensorMap b[DC_MAX_LEVELS];
+};
+
 struct TcParams {
     dc::Geom g;
+    LevelBox box[DC_MAX_LEVELS];
     const int* ii;
     const int* jj;
     int max_frames;
@@ -108,7 +138,7 @@ struct TileInfo {
 };
 
 struct Layout {
-    uint32_t a, b, stage_b, win, st, sched, tinfo, coords, bars, misc, total;
+    uint32_t a, b, stage_b, win, sched, tinfo, bars, misc, total;
 };
 
 __host__ __device__ constexpr Layout make_layout(int atoms) {
@@ -117,11 +147,9 @@ __host__ __device__ constexpr Layout make_layout(int atoms) {
     L.b = L.a + atoms * kTileM * kRowBytes;
     L.stage_b = atoms * kChunkN * kRowBytes;
     L.win = L.b + kStagesB * L.stage_b;
-    L.st = L.win + kTileM * kWinStride * 4;
-    L.sched = L.st;                                          // [2][levels] LevelSched
+    L.sched = L.win + kTileM * kWinStride * 4;               // [2][levels] LevelSched
     L.tinfo = L.sched + 2 * DC_MAX_LEVELS * sizeof(LevelSched);
-    L.coords = L.tinfo + 2 * sizeof(TileInfo);              // [2][2][128] floats
-    L.bars = L.coords + 2 * 2 * kTileM * 4;
+    L.bars = L.tinfo + 2 * sizeof(TileInfo);
     L.misc = L.bars + 24 * 8;
     L.total = L.misc + 64;
     return L;
@@ -136,6 +164,8 @@ enum { kBarAFull = 0, kBarAEmpty = 1, kBarFull = 2, kBarEmpty = kBarFull + kStag
        kBarTFull = kBarEmpty + kStagesB, kBarTEmpty = kBarTFull + kAcc,
        kBarSFull = kBarTEmpty + kAcc, kBarSEmpty = kBarSFull + 2 };
 static_assert(kBarSEmpty + 2 <= 24, "barrier slots");
+// a tile's schedule is released by the producer, the MMA warp and every epilogue warp
+constexpr int kSchedConsumers = 2 + kEpiWarps;
 
 __device__ __forceinline__ void raise_abort(volatile int* abort, int* err, int code) {
     *abort = 1;
@@ -143,9 +173,15 @@ __device__ __forceinline__ void raise_abort(volatile int* abort, int* err, int c
 }
 
 // Optional phase timers (build with -DDC_TC_PROFILE; compiled out otherwise):
-// per CTA, cycles spent in each role's waits and in the epilogue phases.
+// per CTA, cycles spent in each role's waits and in the epilogue phases, and a
+// per-chunk event trace of CTA 0.
 #ifdef DC_TC_PROFILE
 __device__ unsigned long long g_tc_prof[8192 * 16];
+__device__ long long g_tc_trace[8 * 1024];
+#define DC_TRACE(ev, idx)                                                                  \
+    do {                                                                                   \
+        if (blockIdx.x == 0 && (idx) < 1024) g_tc_trace[(ev) * 1024 + (idx)] = clock64(); \
+    } while (0)
 #define DC_PROF_NOW() clock64()
 #define DC_PROF_STORE(slot, v)                                                    \
     do {                                                                          \
@@ -153,6 +189,9 @@ __device__ unsigned long long g_tc_prof[8192 * 16];
         if (cta_ < 8192) g_tc_prof[cta_ * 16 + (slot)] = (unsigned long long)(v); \
     } while (0)
 #else
+#define DC_TRACE(ev, idx) \
+    do {                  \
+    } while (0)
 #define DC_PROF_NOW() 0ll
 #define DC_PROF_STORE(slot, v) \
     do {                       \
@@ -176,12 +215,10 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatil
 }
 
 // Persistent: CTA b handles tiles b, b + gridDim.x, ...; tile t = (edge t / tpe,
-// source pixels 128 * (t % tpe) ..).  The producer warp also prepares each
-// tile's coordinates and chunk schedule one tile ahead, so a tile's set-up and
-// its last level's bilinear step overlap the neighbouring tiles' MMAs.
+// source pixels 128 * (t % tpe) ..).
 template <int R>
 __global__ void __launch_bounds__(kThreads, 1)
-    corr_tc_kernel(const __grid_constant__ CUtensorMap tmap, TcParams P) {
+    corr_tc_kernel(const __grid_constant__ TcMaps maps, TcParams P) {
     constexpr int D = 2 * R + 1, NW = 2 * R + 2;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>(
@@ -201,7 +238,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     float* win_base = reinterpret_cast<float*>(base + Ly.win);
     LevelSched* sched_base = reinterpret_cast<LevelSched*>(base + Ly.sched);
     TileInfo* tinfo = reinterpret_cast<TileInfo*>(base + Ly.tinfo);
-    float* scoords = reinterpret_cast<float*>(base + Ly.coords);
     const uint32_t bars = smem_addr(base + Ly.bars);
     int* misc = reinterpret_cast<int*>(base + Ly.misc);
     volatile int* abort = misc + kMiscAbort;
@@ -220,11 +256,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(bar(kBarSFull + b), 1);
-            mbar_init(bar(kBarSEmpty + b), kEpiWarps + 1);
+            mbar_init(bar(kBarSEmpty + b), kSchedConsumers);
         }
         misc[kMiscAbort] = 0;
         fence_mbar_init();
-        tma_prefetch_desc(&tmap);
+        tma_prefetch_desc(&maps.a);
+        for (int l = 0; l < g.levels; l++) tma_prefetch_desc(&maps.b[l]);
     }
     if (warp == 1) {
         tmem_alloc(smem_addr(misc + kMiscTmem), kTmemCols);
@@ -236,11 +273,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = (uint32_t)misc[kMiscTmem];
     long long w_a = 0, w_b = 0, w_c = 0;  // phase cycles (profiling builds)
 
-    if (warp == 0) {
-        // ---- producer: per tile, coordinates + chunk schedule, then the source
-        //      tile and the target-row chunks through TMA
-        int gc = 0, na = 0, i = 0;
-        int a_issued = 0, last_gc = 0;
+    if (warp == kSchedWarp) {
+        // ---- scheduler: per tile, the target rows (and row segments) of each
+        //      level that some window of the tile's pixels touches
+        int i = 0;
         for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x, i++) {
             const int tb = i & 1;
             if (i >= 2 && !warp_wait(bar(kBarSEmpty + tb), ((i >> 1) - 1) & 1, abort, lane)) {
@@ -248,54 +284,66 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
             const int e = t / tpe, p0 = (t - e * tpe) * kTileM;
-            const int si = P.ii[e], sj = P.jj[e];
+            const int si = __ldg(P.ii + e), sj = __ldg(P.jj + e);
             const bool valid = si >= 0 && si < P.max_frames && sj >= 0 && sj < P.max_frames;
-            float* sc = scoords + tb * 2 * kTileM;
-            int lo[DC_MAX_LEVELS], hi[DC_MAX_LEVELS];
+            float cx[kTileM / 32], cy[kTileM / 32];
+#pragma unroll
+            for (int k = 0; k < kTileM / 32; k++) {  // all loads in flight at once
+                const int p = p0 + lane + 32 * k;
+                cx[k] = p < hw ? __ldg(P.coords + (size_t)e * 2 * hw + p) : 0.0f;
+                cy[k] = p < hw ? __ldg(P.coords + (size_t)e * 2 * hw + hw + p) : 0.0f;
+            }
+            int ylo_[DC_MAX_LEVELS], yhi_[DC_MAX_LEVELS], xlo_[DC_MAX_LEVELS],
+                xhi_[DC_MAX_LEVELS];
 #pragma unroll
             for (int l = 0; l < DC_MAX_LEVELS; l++) {
-                lo[l] = 0x7fffffff;
-                hi[l] = -1;
+                ylo_[l] = xlo_[l] = 0x7fffffff;
+                yhi_[l] = xhi_[l] = -1;
             }
 #pragma unroll
             for (int k = 0; k < kTileM / 32; k++) {
-                const int q = lane + 32 * k, p = p0 + q;
-                float cx = 0.0f, cy = 0.0f;
-                if (p < hw) {
-                    cx = __ldg(P.coords + (size_t)e * 2 * hw + p);
-                    cy = __ldg(P.coords + (size_t)e * 2 * hw + hw + p);
-                }
-                sc[q] = cx;
-                sc[kTileM + q] = cy;
-                if (!(valid && p < hw)) continue;
+                if (!(valid && p0 + lane + 32 * k < hw)) continue;
 #pragma unroll
                 for (int l = 0; l < DC_MAX_LEVELS; l++) {
                     if (l >= g.levels) break;
                     const float s = 1.0f / (float)(1 << l);
-                    const int by = (int)floorf(cy * s) - R, bx = (int)floorf(cx * s) - R;
+                    const int by = (int)floorf(cy[k] * s) - R, bx = (int)floorf(cx[k] * s) - R;
                     const int a0 = max(by, 0), a1 = min(by + NW - 1, g.H[l] - 1);
-                    if (a0 <= a1 && bx + NW - 1 >= 0 && bx < g.W[l]) {
-                        lo[l] = min(lo[l], a0);
-                        hi[l] = max(hi[l], a1);
+                    const int b0 = max(bx, 0), b1 = min(bx + NW - 1, g.W[l] - 1);
+                    if (a0 <= a1 && b0 <= b1) {
+                        ylo_[l] = min(ylo_[l], a0);
+                        yhi_[l] = max(yhi_[l], a1);
+                        xlo_[l] = min(xlo_[l], b0);
+                        xhi_[l] = max(xhi_[l], b1);
                     }
                 }
             }
             int n = 0;
 #pragma unroll
             for (int l = 0; l < DC_MAX_LEVELS; l++) {
-                const int ylo = __reduce_min_sync(0xffffffffu, lo[l]);
-                const int yhi = __reduce_max_sync(0xffffffffu, hi[l]);
+                const int ylo = __reduce_min_sync(0xffffffffu, ylo_[l]);
+                const int yhi = __reduce_max_sync(0xffffffffu, yhi_[l]);
+                const int xlo = __reduce_min_sync(0xffffffffu, xlo_[l]);
+                const int xhi = __reduce_max_sync(0xffffffffu, xhi_[l]);
                 LevelSched L;
                 L.first = n;
                 L.count = 0;
                 L.ylo = ylo;
-                L.yhi = yhi;
-                L.W = max(g.W[l], 1);
-                L.rows_per = L.W <= kChunkN ? kChunkN / L.W : 1;
-                L.seg_max = L.W <= kChunkN ? L.W : kChunkN;
-                L.segs = (L.W + L.seg_max - 1) / L.seg_max;
-                if (l < g.levels && ylo <= yhi)
-                    L.count = (yhi - ylo + L.rows_per) / L.rows_per * L.segs;
+                L.nrows = 0;
+                L.sg0 = 0;
+                L.nsg = 1;
+                L.pad0 = L.pad1 = 0;
+                if (l < g.levels && ylo <= yhi) {
+                    const LevelBox& B = P.box[l];
+                    L.nrows = yhi - ylo + 1;
+                    if (B.segs == 1) {
+                        L.count = (L.nrows + B.br - 1) / B.br;
+                    } else {
+                        L.sg0 = xlo / B.wbox;
+                        L.nsg = xhi / B.wbox - L.sg0 + 1;
+                        L.count = L.nrows * L.nsg;
+                    }
+                }
                 n += L.count;
                 if (lane == 0) sched_base[tb * DC_MAX_LEVELS + l] = L;
             }
@@ -311,46 +359,59 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tinfo[tb] = ti;
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(bar(kBarSFull + tb));  // release: schedule, coords
-            if (n == 0) continue;
-            if (lane == 0) {
+            if (lane == 0) mbar_arrive(bar(kBarSFull + tb));  // release: schedule
+        }
+    } else if (warp == 0) {
+        // ---- producer: per tile, the source tile and the target-row chunks
+        //      through TMA (one elected lane)
+        int gc = 0, na = 0, i = 0;
+        int a_issued = 0, last_gc = 0;
+        for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x, i++) {
+            const int tb = i & 1;
+            if (!warp_wait(bar(kBarSFull + tb), (i >> 1) & 1, abort, lane)) {
+                if (lane == 0) raise_abort(abort, P.err, 2);
+                break;
+            }
+            const TileInfo ti = tinfo[tb];
+            const LevelSched* sch = sched_base + tb * DC_MAX_LEVELS;
+            if (lane == 0 && ti.n > 0) {
                 // the single source-tile buffer: wait until the MMAs of the previous
                 // tile that used it are done
                 if (na >= 1 && !mbar_wait(bar(kBarAEmpty), (na - 1) & 1, abort)) {
-                    raise_abort(abort, P.err, 2);
+                    raise_abort(abort, P.err, 3);
                 } else {
                     mbar_arrive_expect_tx(bar(kBarAFull), P.atoms * kTileM * kRowBytes);
-                    const int arow = (int)((long long)si * g.frame_rows + g.row0[0] + p0);
+                    const int arow = (int)((long long)ti.si * g.frame_rows + g.row0[0] + ti.p0);
                     for (int k = 0; k < P.atoms; k++)
-                        tma_load_2d(sA + k * kTileM * kRowBytes, &tmap, k * 64, arow,
+                        tma_load_2d(sA + k * kTileM * kRowBytes, &maps.a, k * 64, arow,
                                     bar(kBarAFull));
                     a_issued = 1;
-                    const LevelSched* sch = sched_base + tb * DC_MAX_LEVELS;
                     int lv = 0;
-                    for (int c = 0; c < n; c++, gc++) {
+                    for (int c = 0; c < ti.n; c++, gc++) {
                         while (c >= sch[lv].first + sch[lv].count) lv++;
                         const int s = gc % kStagesB;
                         const long long t0 = DC_PROF_NOW();
                         if (gc >= kStagesB &&
                             !mbar_wait(bar(kBarEmpty + s), ((gc / kStagesB) - 1) & 1, abort)) {
-                            raise_abort(abort, P.err, 3);
+                            raise_abort(abort, P.err, 4);
                             break;
                         }
                         w_a += DC_PROF_NOW() - t0;
-                        mbar_arrive_expect_tx(bar(kBarFull + s), Ly.stage_b);
-                        const int row = make_chunk(sch[lv], c - sch[lv].first,
-                                                   (long long)sj * g.frame_rows + g.row0[lv]).row;
+                        DC_TRACE(0, gc);
+                        const LevelBox& B = P.box[lv];
+                        const ChunkGeo cg = chunk_geo(sch[lv], B, c - sch[lv].first);
+                        mbar_arrive_expect_tx(bar(kBarFull + s),
+                                              P.atoms * B.wbox * B.br * kRowBytes);
                         for (int k = 0; k < P.atoms; k++)
-                            for (int h = 0; h < kChunkN / kTileM; h++)  // 128-row boxes
-                                tma_load_2d(sB + s * Ly.stage_b + k * kChunkN * kRowBytes +
-                                                h * kTileM * kRowBytes,
-                                            &tmap, k * 64, row + h * kTileM, bar(kBarFull + s));
+                            tma_load_4d(sB + s * Ly.stage_b + k * kChunkN * kRowBytes, &maps.b[lv],
+                                        k * 64, cg.x0, cg.y0, ti.sj, bar(kBarFull + s));
                         last_gc = gc + 1;
                     }
                 }
             }
-            na++;
+            if (ti.n > 0) na++;
             __syncwarp();
+            if (lane == 0) mbar_arrive(bar(kBarSEmpty + tb));
         }
         if (lane == 0) {
             DC_PROF_STORE(4, w_a);
@@ -368,7 +429,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = blockIdx.x; t < ntiles; t += gridDim.x, i++) {
             const int tb = i & 1;
             if (!warp_wait(bar(kBarSFull + tb), (i >> 1) & 1, abort, lane)) {
-                if (lane == 0) raise_abort(abort, P.err, 4);
+                if (lane == 0) raise_abort(abort, P.err, 5);
                 break;
             }
             const TileInfo ti = tinfo[tb];
@@ -376,7 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             if (lane == 0 && ti.n > 0) {
                 if (!mbar_wait(bar(kBarAFull), na & 1, abort)) {
-                    raise_abort(abort, P.err, 5);
+                    raise_abort(abort, P.err, 6);
                     ok = false;
                 } else {
                     tc_fence_after();
@@ -387,23 +448,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const int s = gc % kStagesB, a = gc % kAcc;
                         const long long t0 = DC_PROF_NOW();
                         if (!mbar_wait(bar(kBarFull + s), (gc / kStagesB) & 1, abort)) {
-                            raise_abort(abort, P.err, 6);
+                            raise_abort(abort, P.err, 7);
                             ok = false;
                             break;
                         }
                         const long long t1 = DC_PROF_NOW();
                         w_a += t1 - t0;
+                        DC_TRACE(1, gc);
                         if (gc >= kAcc &&
                             !mbar_wait(bar(kBarTEmpty + a), ((gc / kAcc) - 1) & 1, abort)) {
-                            raise_abort(abort, P.err, 7);
+                            raise_abort(abort, P.err, 8);
                             ok = false;
                             break;
                         }
                         w_b += DC_PROF_NOW() - t1;
+                        DC_TRACE(2, gc);
                         tc_fence_after();
-                        const int nn = make_chunk(sch[lv], c - sch[lv].first, 0).n;
+                        const int nn = chunk_geo(sch[lv], P.box[lv], c - sch[lv].first).n;
                         const uint32_t idesc = idesc_f16(P.ab_fmt, kTileM, nn);
-                        const uint32_t d = tmem + (uint32_t)(a * kChunkN);
+                        const uint32_t d = tmem + (uint32_t)(a * kAccCols);
                         for (int kk = 0; kk < ksteps; kk++) {
                             const int at = kk >> 2, wi = kk & 3;
                             const uint64_t ad = sdesc_sw128(sA + at * kTileM * kRowBytes + wi * 32);
@@ -413,6 +476,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                         mma_commit(bar(kBarEmpty + s));
                         mma_commit(bar(kBarTFull + a));
+                        DC_TRACE(3, gc);
                     }
                     mma_commit(bar(kBarAEmpty));  // the source tile may be replaced
                 }
@@ -431,20 +495,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
     } else {
         // ---- epilogue: the kSubWarps warps of a TMEM lane quarter take the
-        //      32-column passes of each chunk and split the outputs
+        //      32-column loads of each chunk round-robin and split the outputs
         const int quarter = warp & 3;       // TMEM lane quarter of this warp
-        const int sub = (warp - 2) >> 2;    // which columns of a chunk (0..kSubWarps-1)
+        const int sub = (warp - 2) >> 2;    // which loads / output columns (0..kSubWarps-1)
         const int ti_px = 32 * quarter + lane;
         float* win = win_base + ti_px * kWinStride;
+        const int swz = ti_px & 3;  // unit swizzle of this pixel's window rows
         const uint32_t tl = tmem + ((uint32_t)(32 * quarter) << 16);
-        const int cwarp = kSubCols * kPasses * sub;  // first chunk column of this warp
         int gc = 0, i = 0;
         bool alive = true;
+        // this pixel's coordinates, loaded one tile ahead
+        auto load_coords = [&](int tt, float& x, float& y) {
+            x = y = 0.0f;
+            if (tt < ntiles) {
+                const int e = tt / tpe, q = (tt - e * tpe) * kTileM + ti_px;
+                if (q < hw) {
+                    x = __ldg(P.coords + (size_t)e * 2 * hw + q);
+                    y = __ldg(P.coords + (size_t)e * 2 * hw + hw + q);
+                }
+            }
+        };
+        float cx_next, cy_next;
+        load_coords(blockIdx.x, cx_next, cy_next);
         for (int t = blockIdx.x; t < ntiles && alive; t += gridDim.x, i++) {
             const int tb = i & 1;
+            const float cx = cx_next, cy = cy_next;
+            load_coords(t + gridDim.x, cx_next, cy_next);
             const long long t0s = DC_PROF_NOW();
             if (!warp_wait(bar(kBarSFull + tb), (i >> 1) & 1, abort, lane)) {
-                if (lane == 0) raise_abort(abort, P.err, 8);
+                if (lane == 0) raise_abort(abort, P.err, 9);
                 break;
             }
             w_a += DC_PROF_NOW() - t0s;
@@ -453,10 +532,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int p = tinf.p0 + ti_px;
             const bool pv = p < hw;
             const bool valid = tinf.valid != 0;
-            const float cx = scoords[tb * 2 * kTileM + ti_px];
-            const float cy = scoords[tb * 2 * kTileM + kTileM + ti_px];
             float* out_e = P.out + (size_t)tinf.e * nch * hw;
-            int cend = 0;
             for (int l = 0; l < g.levels && alive; l++) {
                 const int Hl = g.H[l], Wl = g.W[l];
                 const float scale = 1.0f / (float)(1 << l);
@@ -468,79 +544,74 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int xlo = max(bx, 0), xhi = min(bx + NW - 1, Wl - 1);
                 const bool any = valid && pv && ylo <= yhi && xlo <= xhi;
                 const LevelSched Ls = sch[l];
-                const float inv_seg_max = 1.0f / (float)Ls.seg_max;
-                cend += Ls.count;
+                const LevelBox B = P.box[l];
+                // the window's first column lies in strip s0 (at column kx of it);
+                // strips s0 and s0 + 1 go to window slots 0 and 1
+                const int s0 = bx >> 3, kx = bx & 7;
                 for (int c = 0; c < Ls.count; c++, gc++) {
                     const int a = gc % kAcc;
                     const long long t0 = DC_PROF_NOW();
                     if (!warp_wait(bar(kBarTFull + a), (gc / kAcc) & 1, abort, lane)) {
-                        if (lane == 0) raise_abort(abort, P.err, 9);
+                        if (lane == 0) raise_abort(abort, P.err, 10);
                         alive = false;
                         break;
                     }
                     tc_fence_after();
                     const long long t1 = DC_PROF_NOW();
                     w_a += t1 - t0;
-                    const ChunkDesc ch = make_chunk(Ls, c, 0);
-                    const float inv_seg =
-                        ch.seg == Ls.seg_max ? inv_seg_max : 1.0f / (float)ch.seg;
+                    if (lane == 0 && warp == 2) DC_TRACE(4, gc);
+                    if (lane == 0 && warp == 17) DC_TRACE(6, gc);
+                    const ChunkGeo cg = chunk_geo(Ls, B, c);
+                    const int nloads = (cg.cols + kLoadCols - 1) / kLoadCols;
+                    for (int j = sub; j < nloads; j += kSubWarps) {
+                        // the load's four strips: window row and slot of each, or
+                        // out of this pixel's window
+                        int wr[4], slot[4];
+                        bool need_k[4], need = false;
 #pragma unroll
-                    for (int pass = 0; pass < kPasses; pass++) {
-                        const int cb = cwarp + kSubCols * pass;
-                        if (cb >= ch.cols) continue;
-                        const int rlo = div_small(cb, inv_seg);
-                        const int rhi = div_small(min(ch.cols - 1, cb + kSubCols - 1), inv_seg);
-                        // window rows of this pixel inside this pass's chunk rows; tap
-                        // (x, y) sits at staged column (y - y0) * seg + (x - x0) - cb
-                        const int ya = max(ylo, ch.y0 + rlo);
-                        const int yb = min(yhi, ch.y0 + rhi);
-                        const int xa = max(xlo, ch.x0), xb = min(xhi, ch.x0 + ch.seg - 1);
-                        bool need = any && ya <= yb && xa <= xb;
-#if defined(DC_TC_EXP) && DC_TC_EXP == 2
-                        need = false;
-#endif
+                        for (int k = 0; k < 4; k++) {
+                            const int n = j * kLoadCols + k * kStrip;
+                            const int r = div_small(n, B.inv_wbox);
+                            const int x = cg.x0 + n - r * B.wbox;
+                            wr[k] = cg.y0 + r - by;
+                            slot[k] = (x >> 3) - s0;
+                            need_k[k] = any && n < cg.cols && (unsigned)wr[k] < (unsigned)NW &&
+                                        (unsigned)slot[k] < 2u;
+                            need |= need_k[k];
+                        }
                         if (!__any_sync(0xffffffffu, need)) continue;
-                        float v[kSubCols];
-                        tmem_ld32(tl + (uint32_t)(a * kChunkN + cb), v);
-#if defined(DC_TC_EXP) && DC_TC_EXP == 1
-                        if (v[5] != 1234.5f) continue;
-#endif
-                        if (!need) continue;
-                        const int kofs = -ch.x0 - cb;
-                        const int ia = xa - bx, ib = xb - bx;  // valid tap range
-                        for (int y = ya; y <= yb; y++) {
-                            const int k0 = (y - ch.y0) * ch.seg + bx + kofs;
-                            const int lo = max(ia, -k0), hi = min(ib, kSubCols - 1 - k0);
-                            if (lo > hi) continue;
-                            const unsigned span = (unsigned)(hi - lo);
-                            // tap q sits at column k0 + q; the tap whose column is
-                            // congruent to r mod 8 is in register 8 * (column >> 3) + r,
-                            // so each of the 8 residues needs only a 4-way select
-                            float* wcol = win + (y - by);
+                        float v[kLoadCols];
+                        tmem_ld32(tl + (uint32_t)(a * kAccCols + j * kLoadCols), v);
 #pragma unroll
-                            for (int r = 0; r < 8; r++) {
-                                const int q = (r - k0) & 7;
-                                const int kk = (k0 + q) >> 3;
-                                const float val = (kk & 2) ? ((kk & 1) ? v[24 + r] : v[16 + r])
-                                                           : ((kk & 1) ? v[8 + r] : v[r]);
-                                if ((unsigned)(q - lo) <= span) wcol[q * 8] = g.alpha * val;
+                        for (int k = 0; k < 4; k++) {
+                            if (need_k[k]) {
+                                float4* d4 = reinterpret_cast<float4*>(win + wr[k] * kWinRow);
+                                const int u = 2 * slot[k];
+                                d4[u ^ swz] = make_float4(v[8 * k + 0], v[8 * k + 1],
+                                                          v[8 * k + 2], v[8 * k + 3]);
+                                d4[(u + 1) ^ swz] = make_float4(v[8 * k + 4], v[8 * k + 5],
+                                                                v[8 * k + 6], v[8 * k + 7]);
                             }
                         }
                     }
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(bar(kBarTEmpty + a));
+                    if (lane == 0 && warp == 2) DC_TRACE(5, gc);
+                    if (lane == 0 && warp == 17) DC_TRACE(7, gc);
                     w_b += DC_PROF_NOW() - t1;
                 }
                 if (!alive) break;
                 const long long t2 = DC_PROF_NOW();
-                quarter_sync(quarter);  // all passes have written this level's windows
+                quarter_sync(quarter);  // all strips of this level are in the windows
                 if (pv) {
                     bool vy[NW];
 #pragma unroll
                     for (int k = 0; k < NW; k++)
                         vy[k] = any && (unsigned)(by + k) < (unsigned)Hl;
-                    const float ux = 1.0f - dx, uy = 1.0f - dy;
+                    // window values are raw dot products: alpha goes into the x weights
+                    const float ux = g.alpha * (1.0f - dx), vx_w = g.alpha * dx;
+                    const float uy = 1.0f - dy;
                     float* ol = out_e + (size_t)(l * D * D) * hw + p;
                     // the quarter's warps split the output columns a (2, 2, 2, 1 at R = 3)
                     constexpr int AW = (D + kSubWarps - 1) / kSubWarps;
@@ -551,13 +622,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                     float pu[AW + 1][NW], pd[AW + 1][NW];
 #pragma unroll
                     for (int ii = 0; ii <= AW; ii++) {
-                        const int ix = a0 + ii;
-                        const bool vx = ix < NW && (unsigned)(bx + ix) < (unsigned)Wl;
+                        const int ix = min(a0 + ii, NW - 1);
+                        const bool vx = a0 + ii < NW && (unsigned)(bx + ix) < (unsigned)Wl;
+                        // window column ix = row column kx + ix (0..14), swizzled unit
+                        const int col = kx + ix;
+                        const float* wc = win + (((col >> 2) ^ swz) << 2) + (col & 3);
 #pragma unroll
                         for (int j = 0; j < NW; j++) {
-                            const float tt = (vx && vy[j]) ? win[ix * 8 + j] : 0.0f;
+                            const float tt = (vx && vy[j]) ? wc[j * kWinRow] : 0.0f;
                             pu[ii][j] = tt * ux;
-                            pd[ii][j] = tt * dx;
+                            pd[ii][j] = tt * vx_w;
                         }
                     }
 #pragma unroll
@@ -578,7 +652,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 quarter_sync(quarter);  // all are done reading before the next level
                 w_c += DC_PROF_NOW() - t2;
             }
-            (void)cend;
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(kBarSEmpty + tb));
         }
@@ -616,11 +689,27 @@ EncodeTiledFn get_encode() {
     return fn;
 }
 
+// Target boxes of level l: rows padded to a multiple of 8 pixels; a box holds
+// as many whole rows as fit in kChunkN targets, or one kChunkN-wide segment of
+// a wider row.
+LevelBox level_box(const dc_ctx* ctx, int l) {
+    LevelBox b;
+    const int wpad = (ctx->W[l] + kStrip - 1) / kStrip * kStrip;
+    b.wbox = wpad < kChunkN ? wpad : kChunkN;
+    b.br = kChunkN / b.wbox;
+    b.segs = (wpad + b.wbox - 1) / b.wbox;
+    b.inv_wbox = 1.0f / (float)b.wbox;
+    return b;
+}
+
 }  // namespace
 
 #ifdef DC_TC_PROFILE
 extern "C" int dc_tc_profile_read(unsigned long long* host, int n) {
     return (int)cudaMemcpyFromSymbol(host, g_tc_prof, sizeof(unsigned long long) * n);
+}
+extern "C" int dc_tc_trace_read(long long* host) {
+    return (int)cudaMemcpyFromSymbol(host, g_tc_trace, sizeof(long long) * 8 * 1024);
 }
 #endif
 
@@ -630,27 +719,44 @@ bool dc_tc_supported(const dc_ctx* ctx) {
            (ctx->cfg.channels == 64 || ctx->cfg.channels == 128);
 }
 
-// Tensor map over the store, [max_frames * frame_rows][C] 16-bit elements, with
-// boxes of 128 rows x 64 elements (128 bytes) and 128-byte swizzle: the
-// canonical K-major operand layout of tcgen05, for A tiles and B chunks alike.
+// Tensor maps over the store of 16-bit elements, all with 128-byte swizzle (the
+// canonical K-major operand layout of tcgen05): A = [max_frames * frame_rows][C]
+// with boxes of 128 rows x 64 channels; B[l] = level l as the 4-D tensor
+// [slot][H_l][W_l][C] (a slot's level-l rows start at level_row0[l], slots are
+// frame_rows apart) with boxes of br rows x wbox pixels x 64 channels, pixels
+// outside the level reading as zeros (out-of-bounds fill).
 int dc_tc_prepare(dc_ctx* ctx) {
     EncodeTiledFn enc = get_encode();
     if (!enc) return dc_fail(ctx, DC_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
     const CUtensorMapDataType dt = ctx->cfg.precision == DC_PREC_BF16
                                        ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                        : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const size_t row_bytes = (size_t)ctx->cfg.channels * 2;
     cuuint64_t dims[2] = {(cuuint64_t)ctx->cfg.channels,
                           (cuuint64_t)ctx->cfg.max_frames * ctx->frame_rows};
-    cuuint64_t strides[1] = {(cuuint64_t)ctx->cfg.channels * 2};
+    cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
     cuuint32_t estr[2] = {1, 1};
-    static_assert(kChunkN % kTileM == 0, "B chunks are whole 128-row boxes");
     cuuint32_t box[2] = {64, (cuuint32_t)kTileM};
     CUresult r1 = enc(reinterpret_cast<CUtensorMap*>(ctx->tmap_a), dt, 2, ctx->store, dims,
                       strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                       CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r1 != CUDA_SUCCESS)
-        return dc_fail(ctx, DC_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+    if (r1 != CUDA_SUCCESS) return dc_fail(ctx, DC_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+    for (int l = 0; l < ctx->cfg.levels; l++) {
+        const LevelBox lb = level_box(ctx, l);
+        cuuint64_t d4[4] = {(cuuint64_t)ctx->cfg.channels, (cuuint64_t)ctx->W[l],
+                            (cuuint64_t)ctx->H[l], (cuuint64_t)ctx->cfg.max_frames};
+        cuuint64_t s4[3] = {(cuuint64_t)row_bytes, (cuuint64_t)ctx->W[l] * row_bytes,
+                            (cuuint64_t)ctx->frame_rows * row_bytes};
+        cuuint32_t b4[4] = {64, (cuuint32_t)lb.wbox, (cuuint32_t)lb.br, 1};
+        cuuint32_t e4[4] = {1, 1, 1, 1};
+        void* base = static_cast<char*>(ctx->store) + ctx->level_row0[l] * row_bytes;
+        CUresult r = enc(reinterpret_cast<CUtensorMap*>(ctx->tmap_b[l]), dt, 4, base, d4, s4, b4,
+                         e4, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS)
+            return dc_fail(ctx, DC_ERR_CUDA, "cuTensorMapEncodeTiled (level rows) failed");
+    }
     ctx->tc_ready = true;
     return DC_OK;
 }
@@ -660,6 +766,8 @@ int dc_launch_tc(dc_ctx* ctx, const int* ii, const int* jj, int M, const float* 
     if (!ctx->tc_ready) return dc_fail(ctx, DC_ERR_NOT_READY, "tensor maps not prepared");
     TcParams P;
     P.g = dc::geom_of(ctx);
+    for (int l = 0; l < DC_MAX_LEVELS; l++)
+        P.box[l] = l < ctx->cfg.levels ? level_box(ctx, l) : LevelBox{8, 1, 1, 0.125f};
     P.ii = ii;
     P.jj = jj;
     P.max_frames = ctx->cfg.max_frames;
@@ -668,17 +776,20 @@ int dc_launch_tc(dc_ctx* ctx, const int* ii, const int* jj, int M, const float* 
     P.err = ctx->dev_err;
     P.atoms = ctx->cfg.channels * 2 / 128;
     P.ab_fmt = ctx->cfg.precision == DC_PREC_BF16 ? 1u : 0u;
+    P.M = M;
     const Layout Ly = make_layout(P.atoms);
     const size_t smem = Ly.total + 1024;
-    P.M = M;
     const int ntiles = (ctx->hw + kTileM - 1) / kTileM * M;
     dim3 grid(ntiles < ctx->num_sms ? ntiles : ctx->num_sms);
-    const CUtensorMap* ta = reinterpret_cast<const CUtensorMap*>(ctx->tmap_a);
-#define DC_TC_LAUNCH(RR)                                                                   \
-    do {                                                                                   \
-        auto k = corr_tc_kernel<RR>;                                                       \
-        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);   \
-        k<<<grid, kThreads, smem, s>>>(*ta, P);                                       \
+    TcMaps maps;
+    memset(&maps, 0, sizeof(maps));
+    memcpy(&maps.a, ctx->tmap_a, sizeof(CUtensorMap));
+    for (int l = 0; l < ctx->cfg.levels; l++) memcpy(&maps.b[l], ctx->tmap_b[l], sizeof(CUtensorMap));
+#define DC_TC_LAUNCH(RR)                                                                 \
+    do {                                                                                 \
+        auto k = corr_tc_kernel<RR>;                                                     \
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+        k<<<grid, kThreads, smem, s>>>(maps, P);                                         \
     } while (0)
     switch (ctx->cfg.radius) {
         case 0: DC_TC_LAUNCH(0); break;
