@@ -5,9 +5,9 @@
 // one tile of 128 source pixels p, the lookup needs, per level l, the volume
 // values V_l[p][q] = alpha * <f_ii[:, p], P_l f_jj[:, q]> at the (2r+2)^2 taps
 // around each pixel's scaled coordinate.  Per tile:
-//   1. a scheduler warp reduces, over the tile's 128 pixels, the range of target
-//      rows (and, for rows wider than 256 pixels, of row segments) any window of
-//      level l touches, one tile ahead of the others;
+//   1. the producer warp reduces, over the tile's 128 pixels (coordinates
+//      loaded one tile ahead), the range of target rows (and, for rows wider
+//      than 256 pixels, of row segments) any window of level l touches;
 //   2. the producer streams those rows of the pooled target map P_l f_jj
 //      (pixel-major store, K-major operand) into shared memory: one 4-D TMA box
 //      per 64-channel K atom holds `br` whole rows of `wbox` pixels (rows padded
@@ -17,9 +17,10 @@
 //   3. one thread computes each 128 x N x C chunk with tcgen05.mma (kind::f16,
 //      fp16 or bf16 operands, fp32 accumulation in TMEM, two accumulators so the
 //      epilogue of one chunk overlaps the MMAs of the next);
-//   4. the epilogue reads the accumulator in 32-column loads (tcgen05.ld); each
-//      load is four 8-column strips, every strip 8 consecutive target pixels of
-//      one row starting at a multiple of 8.  A window of 8 columns starting at
+//   4. the epilogue drains each chunk in 32-column loads (tcgen05.ld) of four
+//      8-column strips, every strip 8 consecutive target pixels of one row
+//      starting at a multiple of 8; a lane's window needs, per chunk row, at
+//      most two strips (a 32-bit mask over the chunk's strips).  A window of 8 columns starting at
 //      bx touches only strips bx/8 and bx/8 + 1, so a lane copies a strip it
 //      needs into slot 0 or 1 of its window row with two 16-byte stores -- no
 //      per-tap selection;
@@ -28,11 +29,11 @@
 //      column x at slot column (bx mod 8) + x, and stores them as
 //      out[e][l*(2r+1)^2 + a*(2r+1) + b][p] (consecutive pixels per warp).
 //
-// Warp roles (608 threads): warp 0 issues TMA, warp 1 allocates TMEM and issues
-// MMAs (one elected lane each), warps 2..17 are the epilogue, warp 18 schedules
-// tiles.  Warp w reads TMEM lanes 32*(w%4) .. 32*(w%4)+31, i.e. tile pixels
-// 32*(w%4) + lane; the four warps of a lane quarter take a chunk's 32-column
-// loads round-robin and split the bilinear outputs by column.
+// Warp roles (576 threads): warp 0 schedules tiles and issues TMA, warp 1
+// allocates TMEM and issues MMAs (one elected lane each), warps 2..17 are the
+// epilogue.  Warp w reads TMEM lanes 32*(w%4) .. 32*(w%4)+31, i.e. tile pixels
+// 32*(w%4) + lane; the four warps of a lane quarter take 64 columns of every
+// chunk each and split the bilinear outputs by column.
 //
 // Every mbarrier wait is bounded (2 s); on a time-out the CTA raises the
 // context's device error word, stops all roles, waits (bounded) for its TMA
@@ -51,14 +52,13 @@ using namespace dc::sm100;
 constexpr int kTileM = 128;      // source pixels per CTA = MMA M = TMEM lanes
 constexpr int kChunkN = 256;     // max targets per chunk = MMA N
 constexpr int kStrip = 8;        // target pixels per strip
-constexpr int kLoadCols = 32;    // TMEM columns per epilogue load (4 strips)
+constexpr int kChunkStrips = kChunkN / kStrip;  // 32 strips per chunk
 constexpr int kStagesB = 2;      // shared-memory stages of target rows
 constexpr int kAcc = 2;          // TMEM accumulators
 constexpr int kAccCols = 256;    // TMEM columns per accumulator
 constexpr int kSubWarps = 4;     // epilogue warps per TMEM lane quarter
 constexpr int kEpiWarps = 4 * kSubWarps;
-constexpr int kSchedWarp = 2 + kEpiWarps;
-constexpr int kThreads = 32 * (kSchedWarp + 1);
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kWinRow = 16;      // floats per window row: two 8-column strip slots
 constexpr int kWinStride = 8 * kWinRow;      // floats per pixel
 // Within a window row the four 16-byte units (slot 0 low/high, slot 1 low/high)
@@ -67,6 +67,8 @@ constexpr int kWinStride = 8 * kWinRow;      // floats per pixel
 constexpr uint32_t kTmemCols = kAcc * kAccCols;
 constexpr uint32_t kRowBytes = 128;  // one 128-byte K atom per operand row
 static_assert(kChunkN <= kAccCols && kChunkN % 16 == 0, "MMA N");
+static_assert(kChunkStrips == 32, "one bit per strip of a chunk");
+static_assert((kSubWarps & (kSubWarps - 1)) == 0, "chunks rotate over a power of two");
 
 // Per-level constants of the target boxes (host-computed): a box holds br rows
 // of wbox pixels (wbox a multiple of 8, br * wbox <= 256); a row wider than
@@ -138,7 +140,7 @@ struct TileInfo {
 };
 
 struct Layout {
-    uint32_t a, b, stage_b, win, sched, tinfo, bars, misc, total;
+    uint32_t a, b, stage_b, win, sched, tinfo, bars, misc, strips, reps, total;
 };
 
 __host__ __device__ constexpr Layout make_layout(int atoms) {
@@ -151,7 +153,9 @@ __host__ __device__ constexpr Layout make_layout(int atoms) {
     L.tinfo = L.sched + 2 * DC_MAX_LEVELS * sizeof(LevelSched);
     L.bars = L.tinfo + 2 * sizeof(TileInfo);
     L.misc = L.bars + 24 * 8;
-    L.total = L.misc + 64;
+    L.strips = L.misc + 64;                                  // [levels][32] int
+    L.reps = L.strips + DC_MAX_LEVELS * kChunkStrips * 4;    // [levels][33] uint
+    L.total = L.reps + DC_MAX_LEVELS * (kChunkStrips + 1) * 4;
     return L;
 }
 static_assert(make_layout(2).total + 1024 <= 227 * 1024, "shared memory budget");
@@ -164,8 +168,9 @@ enum { kBarAFull = 0, kBarAEmpty = 1, kBarFull = 2, kBarEmpty = kBarFull + kStag
        kBarTFull = kBarEmpty + kStagesB, kBarTEmpty = kBarTFull + kAcc,
        kBarSFull = kBarTEmpty + kAcc, kBarSEmpty = kBarSFull + 2 };
 static_assert(kBarSEmpty + 2 <= 24, "barrier slots");
-// a tile's schedule is released by the producer, the MMA warp and every epilogue warp
-constexpr int kSchedConsumers = 2 + kEpiWarps;
+// a tile's schedule (written by the producer) is released by the MMA warp and
+// every epilogue warp
+constexpr int kSchedConsumers = 1 + kEpiWarps;
 
 __device__ __forceinline__ void raise_abort(volatile int* abort, int* err, int code) {
     *abort = 1;
@@ -198,11 +203,6 @@ __device__ long long g_tc_trace[8 * 1024];
     } while (0)
 #endif
 
-// Named barrier of the kSubWarps epilogue warps that share a TMEM lane quarter.
-__device__ __forceinline__ void quarter_sync(int quarter) {
-    asm volatile("bar.sync %0, %1;" ::"r"(1 + quarter), "r"(32 * kSubWarps) : "memory");
-}
-
 // All lanes of a warp wait for one barrier phase: lane 0 polls (bounded), the
 // others then observe the completed phase.  Returns false on a time-out.
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort,
@@ -212,6 +212,67 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatil
     ok = __shfl_sync(0xffffffffu, ok, 0);
     if (ok) mbar_wait(bar, parity, abort);
     return ok != 0;
+}
+
+// Named barrier of the kSubWarps epilogue warps that share a TMEM lane quarter.
+// Every epilogue warp waits for every accumulator phase, so a time-out ends all
+// of them at the same chunk, before either meeting of that level: no warp is
+// ever left alone at this barrier.
+__device__ __forceinline__ void quarter_sync(int quarter) {
+    asm volatile("bar.sync %0, %1;" ::"r"(1 + quarter), "r"(32 * kSubWarps) : "memory");
+}
+
+// Bilinear outputs of one pixel and level for output columns a0 .. a0 + AW - 1
+// (the window columns are x offsets a, the rows y offsets b), in the
+// reference's order of accumulation (batch_corr_sample_kernel,
+// main.cu:1196-1213): taps (a,b), (a,b+1), (a+1,b), (a+1,b+1), each as
+// fmaf(tap * wx, wy, acc) from +0.  The window holds raw dot products, so alpha
+// rides on the x weights.  kCheck: some taps may lie outside the level; they
+// read as +0, which leaves every fmaf unchanged, as skipping them does in the
+// reference; so do all taps of a pixel with no window in the level (any false).
+// Output column a streams column a times (1 - dx) and column a + 1
+// times dx.
+template <int R, int AW, bool kCheck>
+__device__ __forceinline__ void bilinear_columns(const float* win, int swz, int kx, int a0, int bx,
+                                                 int by, int Wl, int Hl, bool any, float dx,
+                                                 float dy, float alpha, float* ol, int hw) {
+    constexpr int D = 2 * R + 1, NW = 2 * R + 2;
+    bool vy[NW];
+#pragma unroll
+    for (int k = 0; k < NW; k++) vy[k] = !kCheck || (any && (unsigned)(by + k) < (unsigned)Hl);
+    const float ux = alpha * (1.0f - dx), vx_w = alpha * dx;
+    const float uy = 1.0f - dy;
+    float pu[NW];
+#pragma unroll
+    for (int ii = 0; ii <= AW; ii++) {
+        const int ix = min(a0 + ii, NW - 1);
+        const bool vx = a0 + ii < NW && (!kCheck || (unsigned)(bx + ix) < (unsigned)Wl);
+        // window column ix = row column kx + ix (0..14), swizzled unit
+        const int col = kx + ix;
+        const float* wc = win + (((col >> 2) ^ swz) << 2) + (col & 3);
+        float tap[NW];
+#pragma unroll
+        for (int j = 0; j < NW; j++) {
+            if (kCheck)
+                tap[j] = (vx && vy[j]) ? wc[j * kWinRow] : 0.0f;
+            else
+                tap[j] = wc[j * kWinRow];
+        }
+        if (ii > 0 && a0 + ii - 1 < D) {
+            float* o = ol + (size_t)((a0 + ii - 1) * D) * hw;
+#pragma unroll
+            for (int b = 0; b < D; b++) {
+                float acc = fmaf(pu[b], uy, 0.0f);
+                acc = fmaf(pu[b + 1], dy, acc);
+                acc = fmaf(tap[b] * vx_w, uy, acc);
+                acc = fmaf(tap[b + 1] * vx_w, dy, acc);
+                __stcs(o, acc);
+                o += hw;
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < NW; j++) pu[j] = tap[j] * ux;
+    }
 }
 
 // Persistent: CTA b handles tiles b, b + gridDim.x, ...; tile t = (edge t / tpe,
@@ -267,32 +328,73 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_alloc(smem_addr(misc + kMiscTmem), kTmemCols);
         tmem_relinquish();
     }
+    // Per-level tables of the chunk strips (strip q = TMEM columns 8q .. 8q + 7):
+    // strip_tab[l][q] = its row within the chunk (low half) and its strip within
+    // the row segment (high half); rep_tab[l][r] = the bit mask of strips 0 of
+    // rows 0 .. r - 1 (rows are spr = wbox / 8 strips apart).
+    int* strip_tab = reinterpret_cast<int*>(base + Ly.strips);
+    unsigned* rep_tab = reinterpret_cast<unsigned*>(base + Ly.reps);
+    if (threadIdx.x < DC_MAX_LEVELS * kChunkStrips) {
+        const int l = threadIdx.x / kChunkStrips, n = kStrip * (threadIdx.x % kChunkStrips);
+        const LevelBox& B = P.box[l];
+        const int r = div_small(n, B.inv_wbox);
+        strip_tab[threadIdx.x] = r | (((n - r * B.wbox) >> 3) << 16);
+    } else if (threadIdx.x < DC_MAX_LEVELS * kChunkStrips + DC_MAX_LEVELS * (kChunkStrips + 1)) {
+        const int idx = threadIdx.x - DC_MAX_LEVELS * kChunkStrips;
+        const int l = idx / (kChunkStrips + 1), r = idx % (kChunkStrips + 1);
+        const int spr = P.box[l].wbox / kStrip;
+        unsigned m = 0;
+        for (int i = 0; i < r && i * spr < 32; i++) m |= 1u << (i * spr);
+        rep_tab[idx] = m;
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = (uint32_t)misc[kMiscTmem];
     long long w_a = 0, w_b = 0, w_c = 0;  // phase cycles (profiling builds)
 
-    if (warp == kSchedWarp) {
-        // ---- scheduler: per tile, the target rows (and row segments) of each
-        //      level that some window of the tile's pixels touches
-        int i = 0;
+    if (warp == 0) {
+        // ---- producer: per tile, the schedule (target rows, and row segments, of
+        //      each level that some window of the tile's pixels touches, from
+        //      coordinates loaded one tile ahead), then the source tile and the
+        //      target-row chunks through TMA (one elected lane)
+        int gc = 0, na = 0, i = 0;
+        int a_issued = 0, last_gc = 0;
+        float cxn[kTileM / 32], cyn[kTileM / 32];
+        int sin_ = -1, sjn = -1;
+#define DC_TC_LOAD_COORDS(tt)                                                      \
+    do {                                                                           \
+        _Pragma("unroll") for (int k = 0; k < kTileM / 32; k++) cxn[k] = cyn[k] = 0.0f; \
+        if ((tt) < ntiles) {                                                       \
+            const int e_ = (tt) / tpe, q0_ = ((tt) - e_ * tpe) * kTileM;           \
+            sin_ = __ldg(P.ii + e_);                                               \
+            sjn = __ldg(P.jj + e_);                                                \
+            _Pragma("unroll") for (int k = 0; k < kTileM / 32; k++) {              \
+                const int q_ = q0_ + lane + 32 * k;                                \
+                if (q_ < hw) {                                                     \
+                    cxn[k] = __ldg(P.coords + (size_t)e_ * 2 * hw + q_);           \
+                    cyn[k] = __ldg(P.coords + (size_t)e_ * 2 * hw + hw + q_);      \
+                }                                                                  \
+            }                                                                      \
+        }                                                                          \
+    } while (0)
+        DC_TC_LOAD_COORDS(blockIdx.x);  // all loads of a tile in flight at once
         for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x, i++) {
             const int tb = i & 1;
             if (i >= 2 && !warp_wait(bar(kBarSEmpty + tb), ((i >> 1) - 1) & 1, abort, lane)) {
                 if (lane == 0) raise_abort(abort, P.err, 1);
                 break;
             }
-            const int e = t / tpe, p0 = (t - e * tpe) * kTileM;
-            const int si = __ldg(P.ii + e), sj = __ldg(P.jj + e);
-            const bool valid = si >= 0 && si < P.max_frames && sj >= 0 && sj < P.max_frames;
             float cx[kTileM / 32], cy[kTileM / 32];
 #pragma unroll
-            for (int k = 0; k < kTileM / 32; k++) {  // all loads in flight at once
-                const int p = p0 + lane + 32 * k;
-                cx[k] = p < hw ? __ldg(P.coords + (size_t)e * 2 * hw + p) : 0.0f;
-                cy[k] = p < hw ? __ldg(P.coords + (size_t)e * 2 * hw + hw + p) : 0.0f;
+            for (int k = 0; k < kTileM / 32; k++) {
+                cx[k] = cxn[k];
+                cy[k] = cyn[k];
             }
+            const int si = sin_, sj = sjn;
+            DC_TC_LOAD_COORDS(t + gridDim.x);
+            const int e = t / tpe, p0 = (t - e * tpe) * kTileM;
+            const bool valid = si >= 0 && si < P.max_frames && sj >= 0 && sj < P.max_frames;
             int ylo_[DC_MAX_LEVELS], yhi_[DC_MAX_LEVELS], xlo_[DC_MAX_LEVELS],
                 xhi_[DC_MAX_LEVELS];
 #pragma unroll
@@ -360,18 +462,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(kBarSFull + tb));  // release: schedule
-        }
-    } else if (warp == 0) {
-        // ---- producer: per tile, the source tile and the target-row chunks
-        //      through TMA (one elected lane)
-        int gc = 0, na = 0, i = 0;
-        int a_issued = 0, last_gc = 0;
-        for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x, i++) {
-            const int tb = i & 1;
-            if (!warp_wait(bar(kBarSFull + tb), (i >> 1) & 1, abort, lane)) {
-                if (lane == 0) raise_abort(abort, P.err, 2);
-                break;
-            }
             const TileInfo ti = tinfo[tb];
             const LevelSched* sch = sched_base + tb * DC_MAX_LEVELS;
             if (lane == 0 && ti.n > 0) {
@@ -400,6 +490,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         DC_TRACE(0, gc);
                         const LevelBox& B = P.box[lv];
                         const ChunkGeo cg = chunk_geo(sch[lv], B, c - sch[lv].first);
+#if defined(DC_TC_EXP) && (DC_TC_EXP & 8)
+                        mbar_arrive(bar(kBarFull + s));
+                        last_gc = gc + 1;
+                        continue;
+#endif
                         mbar_arrive_expect_tx(bar(kBarFull + s),
                                               P.atoms * B.wbox * B.br * kRowBytes);
                         for (int k = 0; k < P.atoms; k++)
@@ -411,7 +506,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (ti.n > 0) na++;
             __syncwarp();
-            if (lane == 0) mbar_arrive(bar(kBarSEmpty + tb));
         }
         if (lane == 0) {
             DC_PROF_STORE(4, w_a);
@@ -472,7 +566,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                             const uint64_t ad = sdesc_sw128(sA + at * kTileM * kRowBytes + wi * 32);
                             const uint64_t bd = sdesc_sw128(sB + s * Ly.stage_b +
                                                             at * kChunkN * kRowBytes + wi * 32);
+#if !(defined(DC_TC_EXP) && (DC_TC_EXP & 4))
                             mma_f16(d, ad, bd, idesc, kk > 0 ? 1u : 0u);
+#endif
                         }
                         mma_commit(bar(kBarEmpty + s));
                         mma_commit(bar(kBarTFull + a));
@@ -494,8 +590,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
     } else {
-        // ---- epilogue: the kSubWarps warps of a TMEM lane quarter take the
-        //      32-column loads of each chunk round-robin and split the outputs
+        // ---- epilogue: the kSubWarps warps of a TMEM lane quarter take 64
+        //      columns of every chunk each and split the outputs
         const int quarter = warp & 3;       // TMEM lane quarter of this warp
         const int sub = (warp - 2) >> 2;    // which loads / output columns (0..kSubWarps-1)
         const int ti_px = 32 * quarter + lane;
@@ -505,22 +601,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         int gc = 0, i = 0;
         bool alive = true;
         // this pixel's coordinates, loaded one tile ahead
-        auto load_coords = [&](int tt, float& x, float& y) {
-            x = y = 0.0f;
-            if (tt < ntiles) {
-                const int e = tt / tpe, q = (tt - e * tpe) * kTileM + ti_px;
-                if (q < hw) {
-                    x = __ldg(P.coords + (size_t)e * 2 * hw + q);
-                    y = __ldg(P.coords + (size_t)e * 2 * hw + hw + q);
-                }
-            }
-        };
-        float cx_next, cy_next;
-        load_coords(blockIdx.x, cx_next, cy_next);
+        float cx_next = 0.0f, cy_next = 0.0f;
+#define DC_TC_PIXEL_COORDS(tt)                                               \
+    do {                                                                     \
+        cx_next = cy_next = 0.0f;                                            \
+        if ((tt) < ntiles) {                                                 \
+            const int e_ = (tt) / tpe, q_ = ((tt) - e_ * tpe) * kTileM + ti_px; \
+            if (q_ < hw) {                                                   \
+                cx_next = __ldg(P.coords + (size_t)e_ * 2 * hw + q_);        \
+                cy_next = __ldg(P.coords + (size_t)e_ * 2 * hw + hw + q_);   \
+            }                                                                \
+        }                                                                    \
+    } while (0)
+        DC_TC_PIXEL_COORDS(blockIdx.x);
         for (int t = blockIdx.x; t < ntiles && alive; t += gridDim.x, i++) {
             const int tb = i & 1;
             const float cx = cx_next, cy = cy_next;
-            load_coords(t + gridDim.x, cx_next, cy_next);
+            DC_TC_PIXEL_COORDS(t + gridDim.x);
             const long long t0s = DC_PROF_NOW();
             if (!warp_wait(bar(kBarSFull + tb), (i >> 1) & 1, abort, lane)) {
                 if (lane == 0) raise_abort(abort, P.err, 9);
@@ -548,6 +645,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // the window's first column lies in strip s0 (at column kx of it);
                 // strips s0 and s0 + 1 go to window slots 0 and 1
                 const int s0 = bx >> 3, kx = bx & 7;
+                const int* strip_l = strip_tab + l * kChunkStrips;
+                const unsigned* rep_l = rep_tab + l * (kChunkStrips + 1);
+                const int spr = B.wbox / kStrip;
                 for (int c = 0; c < Ls.count; c++, gc++) {
                     const int a = gc % kAcc;
                     const long long t0 = DC_PROF_NOW();
@@ -560,33 +660,44 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const long long t1 = DC_PROF_NOW();
                     w_a += t1 - t0;
                     if (lane == 0 && warp == 2) DC_TRACE(4, gc);
-                    if (lane == 0 && warp == 17) DC_TRACE(6, gc);
                     const ChunkGeo cg = chunk_geo(Ls, B, c);
-                    const int nloads = (cg.cols + kLoadCols - 1) / kLoadCols;
-                    for (int j = sub; j < nloads; j += kSubWarps) {
-                        // the load's four strips: window row and slot of each, or
-                        // out of this pixel's window
-                        int wr[4], slot[4];
-                        bool need_k[4], need = false;
+                    // bit q of m: strip q of this chunk holds part of this pixel's
+                    // window -- rows ra .. rb of the chunk, strips xs0 and xs0 + 1
+                    // of the row segment
+                    unsigned m = 0;
+                    const int ry = cg.y0 - by, xs0 = s0 - (cg.x0 >> 3);
+                    const int ra = max(-ry, 0), rb = min(NW - 1 - ry, cg.rows - 1);
+                    if (any && ra <= rb) {
+                        const unsigned rr = rep_l[rb + 1] ^ rep_l[ra];
+                        if ((unsigned)xs0 < (unsigned)spr) m |= rr << xs0;
+                        if ((unsigned)(xs0 + 1) < (unsigned)spr) m |= rr << (xs0 + 1);
+                    }
+#if defined(DC_TC_EXP) && (DC_TC_EXP & 1)
+                    const bool need_ld = m != 0;
+                    m = 0;
+#endif
+                    // this warp's two 32-column groups: chunk strips 8 * sub ..
+                    const int ngroups = (cg.cols + 31) >> 5;
+#pragma unroll
+                    for (int hh = 0; hh < 2; hh++) {
+                        const int h = 2 * sub + hh;
+                        if (h >= ngroups) break;
+                        const unsigned nh = (m >> (4 * h)) & 0xfu;
+#if defined(DC_TC_EXP) && (DC_TC_EXP & 1)
+                        if (!__any_sync(0xffffffffu, need_ld)) continue;
+#else
+                        if (!__any_sync(0xffffffffu, nh != 0)) continue;
+#endif
+                        float v[32];
+                        tmem_ld32(tl + (uint32_t)(a * kAccCols + 32 * h), v);
+                        if (lane == 0 && warp == 2) DC_TRACE(5 + hh, gc);
 #pragma unroll
                         for (int k = 0; k < 4; k++) {
-                            const int n = j * kLoadCols + k * kStrip;
-                            const int r = div_small(n, B.inv_wbox);
-                            const int x = cg.x0 + n - r * B.wbox;
-                            wr[k] = cg.y0 + r - by;
-                            slot[k] = (x >> 3) - s0;
-                            need_k[k] = any && n < cg.cols && (unsigned)wr[k] < (unsigned)NW &&
-                                        (unsigned)slot[k] < 2u;
-                            need |= need_k[k];
-                        }
-                        if (!__any_sync(0xffffffffu, need)) continue;
-                        float v[kLoadCols];
-                        tmem_ld32(tl + (uint32_t)(a * kAccCols + j * kLoadCols), v);
-#pragma unroll
-                        for (int k = 0; k < 4; k++) {
-                            if (need_k[k]) {
-                                float4* d4 = reinterpret_cast<float4*>(win + wr[k] * kWinRow);
-                                const int u = 2 * slot[k];
+                            if (nh & (1u << k)) {
+                                const int e = strip_l[4 * h + k];
+                                const int wr = ry + (e & 0xffff);
+                                const int u = 2 * ((e >> 16) - xs0);
+                                float4* d4 = reinterpret_cast<float4*>(win + wr * kWinRow);
                                 d4[u ^ swz] = make_float4(v[8 * k + 0], v[8 * k + 1],
                                                           v[8 * k + 2], v[8 * k + 3]);
                                 d4[(u + 1) ^ swz] = make_float4(v[8 * k + 4], v[8 * k + 5],
@@ -597,57 +708,29 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(bar(kBarTEmpty + a));
-                    if (lane == 0 && warp == 2) DC_TRACE(5, gc);
-                    if (lane == 0 && warp == 17) DC_TRACE(7, gc);
+                    if (lane == 0 && warp == 2) DC_TRACE(7, gc);
                     w_b += DC_PROF_NOW() - t1;
                 }
                 if (!alive) break;
                 const long long t2 = DC_PROF_NOW();
+                // the warp's windows all inside the level: no tap needs a check
+                const bool interior_all = __all_sync(
+                    0xffffffffu, !pv || (any && bx >= 0 && bx + NW - 1 < Wl && by >= 0 &&
+                                         by + NW - 1 < Hl));
                 quarter_sync(quarter);  // all strips of this level are in the windows
+#if defined(DC_TC_EXP) && (DC_TC_EXP & 2)
+                if (false) {
+#else
                 if (pv) {
-                    bool vy[NW];
-#pragma unroll
-                    for (int k = 0; k < NW; k++)
-                        vy[k] = any && (unsigned)(by + k) < (unsigned)Hl;
-                    // window values are raw dot products: alpha goes into the x weights
-                    const float ux = g.alpha * (1.0f - dx), vx_w = g.alpha * dx;
-                    const float uy = 1.0f - dy;
+#endif
+                    constexpr int AW = (D + kSubWarps - 1) / kSubWarps;  // 2, 2, 2, 1 at R = 3
                     float* ol = out_e + (size_t)(l * D * D) * hw + p;
-                    // the quarter's warps split the output columns a (2, 2, 2, 1 at R = 3)
-                    constexpr int AW = (D + kSubWarps - 1) / kSubWarps;
-                    const int a0 = sub * AW;
-                    // taps of columns a0 .. a0 + AW, premultiplied by the x weights;
-                    // taps outside the level read as +0, which leaves every fmaf
-                    // below unchanged, as skipping them does in the reference
-                    float pu[AW + 1][NW], pd[AW + 1][NW];
-#pragma unroll
-                    for (int ii = 0; ii <= AW; ii++) {
-                        const int ix = min(a0 + ii, NW - 1);
-                        const bool vx = a0 + ii < NW && (unsigned)(bx + ix) < (unsigned)Wl;
-                        // window column ix = row column kx + ix (0..14), swizzled unit
-                        const int col = kx + ix;
-                        const float* wc = win + (((col >> 2) ^ swz) << 2) + (col & 3);
-#pragma unroll
-                        for (int j = 0; j < NW; j++) {
-                            const float tt = (vx && vy[j]) ? wc[j * kWinRow] : 0.0f;
-                            pu[ii][j] = tt * ux;
-                            pd[ii][j] = tt * vx_w;
-                        }
-                    }
-#pragma unroll
-                    for (int ai = 0; ai < AW; ai++) {
-                        const int aa = a0 + ai;
-                        if (aa >= D) break;
-#pragma unroll
-                        for (int b = 0; b < D; b++) {
-                            // reference order: taps (a,b), (a,b+1), (a+1,b), (a+1,b+1)
-                            float acc = fmaf(pu[ai][b], uy, 0.0f);
-                            acc = fmaf(pu[ai][b + 1], dy, acc);
-                            acc = fmaf(pd[ai + 1][b], uy, acc);
-                            acc = fmaf(pd[ai + 1][b + 1], dy, acc);
-                            __stcs(ol + (size_t)(aa * D + b) * hw, acc);
-                        }
-                    }
+                    if (interior_all)
+                        bilinear_columns<R, AW, false>(win, swz, kx, sub * AW, bx, by, Wl, Hl,
+                                                       true, dx, dy, g.alpha, ol, hw);
+                    else
+                        bilinear_columns<R, AW, true>(win, swz, kx, sub * AW, bx, by, Wl, Hl, any,
+                                                      dx, dy, g.alpha, ol, hw);
                 }
                 quarter_sync(quarter);  // all are done reading before the next level
                 w_c += DC_PROF_NOW() - t2;
@@ -662,6 +745,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
 
+#undef DC_TC_LOAD_COORDS
+#undef DC_TC_PIXEL_COORDS
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {

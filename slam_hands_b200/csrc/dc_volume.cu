@@ -141,43 +141,70 @@ __device__ __forceinline__ float avg4(float a, float b, float c, float d) {
     return 0.25f * (__fadd_rn(__fadd_rn(__fadd_rn(a, b), c), d));
 }
 
+// Coarser levels of one volume row from its level-0 map in shared memory (the
+// levels lie back to back from sm).
+__device__ __forceinline__ void pyramid_levels(float* sm, const dc::LevelOutPtrs& vols,
+                                               long long row, const dc::Geom& g) {
+    const float* s = sm;
+    float* d = sm + g.H[0] * g.W[0];
+#pragma unroll
+    for (int l = 1; l < DC_MAX_LEVELS; l++) {
+        if (l >= g.levels) break;
+        const int Ws = g.W[l - 1], Wd = g.W[l], nd = g.H[l] * g.W[l];
+        float* out = vols.p[l] ? vols.p[l] + (size_t)row * nd : nullptr;
+        for (int i = threadIdx.x; i < nd; i += blockDim.x) {
+            const int y = i / Wd, x = i - y * Wd;
+            const float v = avg4(s[(2 * y) * Ws + 2 * x], s[(2 * y) * Ws + 2 * x + 1],
+                                 s[(2 * y + 1) * Ws + 2 * x], s[(2 * y + 1) * Ws + 2 * x + 1]);
+            d[i] = v;
+            if (out) out[i] = v;
+        }
+        __syncthreads();
+        s = d;
+        d += nd;
+    }
+}
+
 // Grid-stride over volume rows; each row's level-0 map goes through shared
-// memory once and all coarser levels are produced from it.
+// memory once and all coarser levels are produced from it.  With rows of a
+// multiple of 4 floats, every thread holds KV float4 of the NEXT row in
+// registers while the current row is pooled and stored, so each SM keeps its
+// rows' reads in flight (HBM-bound: one read of V0, one write of V1..V3).
+template <int KV>
 __global__ void __launch_bounds__(256) volume_pyramid_kernel(dc::LevelOutPtrs vols, long long N,
                                                               dc::Geom g) {
     extern __shared__ float sm[];
-    float* lv[DC_MAX_LEVELS];
-    {
-        size_t off = 0;
-        for (int l = 0; l < DC_MAX_LEVELS; l++) {
-            lv[l] = sm + off;
-            off += (size_t)g.H[l] * g.W[l];
-        }
-    }
     const int n0 = g.H[0] * g.W[0];
-    const bool vec = (n0 & 3) == 0;
-    for (long long row = blockIdx.x; row < N; row += gridDim.x) {
-        const float* src = vols.p[0] + (size_t)row * n0;
-        if (vec) {
-            for (int i = threadIdx.x; i < n0 / 4; i += blockDim.x)
-                reinterpret_cast<float4*>(lv[0])[i] = __ldcs(reinterpret_cast<const float4*>(src) + i);
-        } else {
-            for (int i = threadIdx.x; i < n0; i += blockDim.x) lv[0][i] = __ldcs(src + i);
-        }
-        __syncthreads();
-        for (int l = 1; l < g.levels; l++) {
-            const int Hs = g.H[l - 1], Ws = g.W[l - 1], Wd = g.W[l], nd = g.H[l] * g.W[l];
-            float* out = vols.p[l] ? vols.p[l] + (size_t)row * nd : nullptr;
-            for (int i = threadIdx.x; i < nd; i += blockDim.x) {
-                const int y = i / Wd, x = i % Wd;
-                const float* s = lv[l - 1];
-                float v = avg4(s[(2 * y) * Ws + 2 * x], s[(2 * y) * Ws + 2 * x + 1],
-                               s[(2 * y + 1) * Ws + 2 * x], s[(2 * y + 1) * Ws + 2 * x + 1]);
-                lv[l][i] = v;
-                if (out) out[i] = v;
+    if (KV > 0) {
+        const int nv = n0 / 4;
+        float4 r[KV > 0 ? KV : 1];
+        long long row = blockIdx.x;
+#define DC_PYR_FETCH(ROW)                                                                 \
+    do {                                                                                  \
+        const float4* src_ = reinterpret_cast<const float4*>(vols.p[0] + (size_t)(ROW) * n0); \
+        _Pragma("unroll") for (int k = 0; k < KV; k++) {                                  \
+            const int idx = threadIdx.x + k * blockDim.x;                                 \
+            if (idx < nv) r[k] = __ldcs(src_ + idx);                                      \
+        }                                                                                 \
+    } while (0)
+        if (row < N) DC_PYR_FETCH(row);
+        for (; row < N; row += gridDim.x) {
+#pragma unroll
+            for (int k = 0; k < KV; k++) {
+                const int idx = threadIdx.x + k * blockDim.x;
+                if (idx < nv) reinterpret_cast<float4*>(sm)[idx] = r[k];
             }
-            (void)Hs;
             __syncthreads();
+            if (row + gridDim.x < N) DC_PYR_FETCH(row + gridDim.x);  // in flight while pooling
+            pyramid_levels(sm, vols, row, g);
+        }
+#undef DC_PYR_FETCH
+    } else {
+        for (long long row = blockIdx.x; row < N; row += gridDim.x) {
+            const float* src = vols.p[0] + (size_t)row * n0;
+            for (int i = threadIdx.x; i < n0; i += blockDim.x) sm[i] = __ldcs(src + i);
+            __syncthreads();
+            pyramid_levels(sm, vols, row, g);
         }
     }
 }
@@ -231,13 +258,33 @@ int dc_launch_volume_pyramid(dc_ctx* ctx, float* const* vols, int M, cudaStream_
     // requested; the kernel only skips the store.
     size_t smem = 0;
     for (int l = 0; l < DC_MAX_LEVELS; l++) smem += (size_t)g.H[l] * g.W[l] * sizeof(float);
-    if (smem > 48 * 1024)
-        cudaFuncSetAttribute(volume_pyramid_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem);
     long long N = (long long)M * g.hw;
-    long long blocks = (long long)ctx->num_sms * 8;
-    if (blocks > N) blocks = N;
-    volume_pyramid_kernel<<<(unsigned)blocks, 256, smem, s>>>(lp, N, g);
+    const int n0 = g.H[0] * g.W[0];
+    // float4 per thread of one row (256 threads), rounded up to an instantiation
+    const int kv = (n0 & 3) ? 0 : (n0 / 4 + 255) / 256;
+    // persistent: as many CTAs as fit on the device at once
+#define DC_PYR_LAUNCH(KV)                                                                 \
+    do {                                                                                  \
+        if (smem > 48 * 1024)                                                             \
+            cudaFuncSetAttribute(volume_pyramid_kernel<KV>,                               \
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+        int per_sm = 0;                                                                   \
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, volume_pyramid_kernel<KV>, \
+                                                      256, smem);                         \
+        long long blocks = (long long)ctx->num_sms * (per_sm > 0 ? per_sm : 1);           \
+        if (blocks > N) blocks = N;                                                       \
+        volume_pyramid_kernel<KV><<<(unsigned)blocks, 256, smem, s>>>(lp, N, g);          \
+    } while (0)
+    if (kv == 0) DC_PYR_LAUNCH(0);
+    else if (kv <= 1) DC_PYR_LAUNCH(1);
+    else if (kv <= 2) DC_PYR_LAUNCH(2);
+    else if (kv <= 3) DC_PYR_LAUNCH(3);
+    else if (kv <= 4) DC_PYR_LAUNCH(4);
+    else if (kv <= 6) DC_PYR_LAUNCH(6);
+    else if (kv <= 8) DC_PYR_LAUNCH(8);
+    else if (kv <= 12) DC_PYR_LAUNCH(12);
+    else DC_PYR_LAUNCH(16);
+#undef DC_PYR_LAUNCH
     return dc_check_launch(ctx, "volume_pyramid_kernel");
 }
 
