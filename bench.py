@@ -233,12 +233,25 @@ def main():
     vols = ([torch.empty(sh, dtype=torch.float32, device=dev) for sh in dc.volume_shapes(M)]
             if args.materialise else None)
 
-    def corr():
+    stage_ev = []  # materialised path: (build+pyramid start, lookup start, end) per step
+
+    def corr(ii_=None, jj_=None, coords_=None, record=False):
+        ii_ = ii_d if ii_ is None else ii_
+        jj_ = jj_d if jj_ is None else jj_
+        coords_ = coords if coords_ is None else coords_
         if vols is not None:
-            dc.build_volume(ii_d, jj_d, vols)
-            dc.lookup(vols, coords, out)
+            evs = [torch.cuda.Event(enable_timing=True) for _ in range(3)] if record else None
+            if evs:
+                evs[0].record(stream)
+            dc.build_volume(ii_, jj_, vols)
+            if evs:
+                evs[1].record(stream)
+            dc.lookup(vols, coords_, out)
+            if evs:
+                evs[2].record(stream)
+                stage_ev.append(evs)
         else:
-            dc.build_and_lookup(ii_d, jj_d, coords, out)
+            dc.build_and_lookup(ii_, jj_, coords_, out)
 
     def step():
         # rank 0 packs the step's keyframes and broadcasts the packed slots
@@ -275,7 +288,7 @@ def main():
         if pg is not None:
             replicate_store(dc, 0, wl.frames)
         ev[s][2].record(stream)
-        corr()
+        corr(record=True)
         ev[s][3].record(stream)
         ev[s][1].record(stream)
     torch.cuda.synchronize()
@@ -312,7 +325,7 @@ def main():
             dc.set_frames(fm_d2)
         if pg is not None:
             replicate_store(dc, 0, wl.frames)
-        dc.build_and_lookup(ii_d2, jj_d2, coords_d2, out)
+        corr(ii_d2, jj_d2, coords_d2)
         out_h.copy_(out, non_blocking=True)
 
     for _ in range(3):
@@ -352,16 +365,38 @@ def main():
     esz = 2 if args.precision in ("fp16", "bf16") else 4
     uniq_frames = len(set(ii) | set(jj))
     pyr_rows = sum((wl.h >> l) * (wl.w >> l) for l in range(dc.levels))
-    alg_bytes = (M * (2 * hw * 4 + dc.out_channels * hw * 4)       # coords in, output out
-                 + uniq_frames * pyr_rows * wl.channels * esz)     # each store row read once
+    io_bytes = M * (2 * hw * 4 + dc.out_channels * hw * 4)          # coords in, output out
+    frame_bytes = uniq_frames * pyr_rows * wl.channels * esz          # each store row read once
+    stages = None
+    if vols is None:
+        alg_bytes = io_bytes + frame_bytes
+        kernel_name = "build_and_lookup"
+    else:
+        # materialised: V0 written, V0 read back by the pyramid, V1..V3 written,
+        # the lookup's (2r+2)^2 taps per pixel and level read once, output written
+        taps = (2 * dc.radius + 2) ** 2
+        vol_bytes = [M * hw * (wl.h >> l) * (wl.w >> l) * 4 for l in range(dc.levels)]
+        build_bytes = vol_bytes[0] * 2 + sum(vol_bytes[1:]) + frame_bytes
+        lookup_bytes = io_bytes + M * hw * dc.levels * taps * 4
+        alg_bytes = build_bytes + lookup_bytes
+        kernel_name = "build_volume (tcgen05 V0 + pyramid) + lookup"
+        b_ms = sum(a.elapsed_time(b) for a, b, _ in stage_ev) / len(stage_ev)
+        l_ms = sum(b.elapsed_time(c) for _, b, c in stage_ev) / len(stage_ev)
+        stages = {"build_volume_ms": b_ms, "build_volume_alg_bytes": build_bytes,
+                  "build_volume_gbs": build_bytes / (b_ms * 1e-3) / 1e9,
+                  "lookup_ms": l_ms, "lookup_alg_bytes": lookup_bytes,
+                  "lookup_gbs": lookup_bytes / (l_ms * 1e-3) / 1e9}
     achieved = alg_bytes / (kern_ms * 1e-3) / 1e9
     peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     peak, peak_src = 6650.0, "fallback"
     if os.path.exists(peaks_path):
         peak, peak_src = float(json.load(open(peaks_path))["hbm_gbs"]), "measured"
+    if stages is not None:
+        stages["build_volume_frac"] = stages["build_volume_gbs"] / peak
+        stages["lookup_frac"] = stages["lookup_gbs"] / peak
     traffic = None
     tpath = os.path.join(ROOT, "profiles", f"corr_tc_kernel_{wl.name}.md")
-    if os.path.exists(tpath) and args.precision == "fp16":
+    if os.path.exists(tpath) and args.precision == "fp16" and vols is None:
         for ln in open(tpath):
             if ln.startswith("traffic_bytes_per_launch:"):
                 traffic = int(ln.split(":")[1])
@@ -372,19 +407,22 @@ def main():
         "vs_baseline": None, "dtype": args.precision, "data": "synthetic",
         "config": {"workload": f"{wl.name}: {wl.frames} kf {wl.h}x{wl.w}x{wl.channels}, "
                                f"{M} edges per GPU ({wl.mode} workload), build+pyramid+r3 "
-                               "lookup, no volume stored",
+                               + ("lookup, volumes materialised in HBM" if vols is not None
+                                  else "lookup, no volume stored"),
                    "alpha": wl.alpha, "l2": "flushed between steps (252 MB read)",
                    "parallelism": f"edges sharded, dp{world}"},
         "gpu_launches": launches,
         "kernel_ms": kern_ms,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": traffic,
-                     "kernel": "build_and_lookup", "peak_source": peak_src,
+                     "kernel": kernel_name, "peak_source": peak_src,
                      "alg_bytes_per_launch": alg_bytes},
         "e2e": {"value": M * world / (e2e_ms * 1e-3), "unit": UNIT,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
         "clocks": clk,
     }
+    if stages is not None:
+        line["stages"] = stages
 
     # reference kernels on this GPU (cuBLAS FP16 GEMM + pools + lookups), if built
     if not args.no_ref_gpu and world == 1:

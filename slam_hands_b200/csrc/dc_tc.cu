@@ -17,7 +17,7 @@
 //   3. one thread computes each 128 x N x C chunk with tcgen05.mma (kind::f16,
 //      fp16 or bf16 operands, fp32 accumulation in TMEM, two accumulators so the
 //      epilogue of one chunk overlaps the MMAs of the next);
-//   4. the epilogue drains each chunk in 32-column loads (tcgen05.ld) of four
+//   4. the epilogue drains each chunk in 64-column loads (tcgen05.ld) of eight
 //      8-column strips, every strip 8 consecutive target pixels of one row
 //      starting at a multiple of 8; a lane's window needs, per chunk row, at
 //      most two strips (a 32-bit mask over the chunk's strips).  A window of 8 columns starting at
@@ -29,11 +29,11 @@
 //      column x at slot column (bx mod 8) + x, and stores them as
 //      out[e][l*(2r+1)^2 + a*(2r+1) + b][p] (consecutive pixels per warp).
 //
-// Warp roles (576 threads): warp 0 schedules tiles and issues TMA, warp 1
-// allocates TMEM and issues MMAs (one elected lane each), warps 2..17 are the
+// Warp roles (320 threads): warp 0 schedules tiles and issues TMA, warp 1
+// allocates TMEM and issues MMAs (one elected lane each), warps 2..9 are the
 // epilogue.  Warp w reads TMEM lanes 32*(w%4) .. 32*(w%4)+31, i.e. tile pixels
-// 32*(w%4) + lane; the four warps of a lane quarter take 64 columns of every
-// chunk each and split the bilinear outputs by column.
+// 32*(w%4) + lane; the two warps of a lane quarter take 128 columns of every
+// chunk each (two 64-column loads) and split the bilinear outputs by column.
 //
 // Every mbarrier wait is bounded (2 s); on a time-out the CTA raises the
 // context's device error word, stops all roles, waits (bounded) for its TMA
@@ -56,7 +56,11 @@ constexpr int kChunkStrips = kChunkN / kStrip;  // 32 strips per chunk
 constexpr int kStagesB = 2;      // shared-memory stages of target rows
 constexpr int kAcc = 2;          // TMEM accumulators
 constexpr int kAccCols = 256;    // TMEM columns per accumulator
-constexpr int kSubWarps = 4;     // epilogue warps per TMEM lane quarter
+#ifndef DC_TC_SUBWARPS
+#define DC_TC_SUBWARPS 2
+#endif
+constexpr int kSubWarps = DC_TC_SUBWARPS;  // epilogue warps per TMEM lane quarter
+constexpr int kWarpBlocks = 4 / kSubWarps;   // 64-column blocks per epilogue warp and chunk
 constexpr int kEpiWarps = 4 * kSubWarps;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kWinRow = 16;      // floats per window row: two 8-column strip slots
@@ -68,7 +72,7 @@ constexpr uint32_t kTmemCols = kAcc * kAccCols;
 constexpr uint32_t kRowBytes = 128;  // one 128-byte K atom per operand row
 static_assert(kChunkN <= kAccCols && kChunkN % 16 == 0, "MMA N");
 static_assert(kChunkStrips == 32, "one bit per strip of a chunk");
-static_assert((kSubWarps & (kSubWarps - 1)) == 0, "chunks rotate over a power of two");
+static_assert(kSubWarps == 2 || kSubWarps == 4, "a chunk is four 64-column blocks");
 
 // Per-level constants of the target boxes (host-computed): a box holds br rows
 // of wbox pixels (wbox a multiple of 8, br * wbox <= 256); a row wider than
@@ -590,8 +594,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
     } else {
-        // ---- epilogue: the kSubWarps warps of a TMEM lane quarter take 64
-        //      columns of every chunk each and split the outputs
+        // ---- epilogue: the kSubWarps warps of a TMEM lane quarter take
+        //      256 / kSubWarps columns of every chunk each and split the outputs
         const int quarter = warp & 3;       // TMEM lane quarter of this warp
         const int sub = (warp - 2) >> 2;    // which loads / output columns (0..kSubWarps-1)
         const int ti_px = 32 * quarter + lane;
@@ -676,25 +680,24 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const bool need_ld = m != 0;
                     m = 0;
 #endif
-                    // this warp's two 32-column groups: chunk strips 8 * sub ..
-                    const int ngroups = (cg.cols + 31) >> 5;
+                    // this warp's 64-column blocks: chunk strips 8 * (kWarpBlocks * sub + bb) ..
 #pragma unroll
-                    for (int hh = 0; hh < 2; hh++) {
-                        const int h = 2 * sub + hh;
-                        if (h >= ngroups) break;
-                        const unsigned nh = (m >> (4 * h)) & 0xfu;
+                    for (int bb = 0; bb < kWarpBlocks; bb++) {
+                        const int blk = kWarpBlocks * sub + bb;
+                        if (64 * blk >= cg.cols) break;
+                        const unsigned n8 = (m >> (8 * blk)) & 0xffu;
 #if defined(DC_TC_EXP) && (DC_TC_EXP & 1)
                         if (!__any_sync(0xffffffffu, need_ld)) continue;
 #else
-                        if (!__any_sync(0xffffffffu, nh != 0)) continue;
+                        if (!__any_sync(0xffffffffu, n8 != 0)) continue;
 #endif
-                        float v[32];
-                        tmem_ld32(tl + (uint32_t)(a * kAccCols + 32 * h), v);
-                        if (lane == 0 && warp == 2) DC_TRACE(5 + hh, gc);
+                        float v[64];
+                        tmem_ld64(tl + (uint32_t)(a * kAccCols + 64 * blk), v);
+                        if (lane == 0 && warp == 2) DC_TRACE(5 + bb, gc);
 #pragma unroll
-                        for (int k = 0; k < 4; k++) {
-                            if (nh & (1u << k)) {
-                                const int e = strip_l[4 * h + k];
+                        for (int k = 0; k < 8; k++) {
+                            if (n8 & (1u << k)) {
+                                const int e = strip_l[8 * blk + k];
                                 const int wr = ry + (e & 0xffff);
                                 const int u = 2 * ((e >> 16) - xs0);
                                 float4* d4 = reinterpret_cast<float4*>(win + wr * kWinRow);
@@ -723,7 +726,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #else
                 if (pv) {
 #endif
-                    constexpr int AW = (D + kSubWarps - 1) / kSubWarps;  // 2, 2, 2, 1 at R = 3
+                    constexpr int AW = (D + kSubWarps - 1) / kSubWarps;  // 4, 3 at R = 3
                     float* ol = out_e + (size_t)(l * D * D) * hw + p;
                     if (interior_all)
                         bilinear_columns<R, AW, false>(win, swz, kx, sub * AW, bx, by, Wl, Hl,
