@@ -49,6 +49,9 @@ def parse():
     ap.add_argument("--precision", default="fp16", choices=["fp32", "tf32", "bf16", "fp16"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-gpu", action="store_true")
+    ap.add_argument("--project", action="store_true",
+                    help="coordinates from poses + inverse depths inside the step "
+                         "(dc_project_build_and_lookup: reprojection + fused correlation)")
     ap.add_argument("--materialise", action="store_true",
                     help="store the volume pyramid (dc_build_volume) and look up from it, "
                          "the reference's own data flow, instead of the fused path")
@@ -234,6 +237,17 @@ def main():
             if args.materialise else None)
 
     stage_ev = []  # materialised path: (build+pyramid start, lookup start, end) per step
+    proj = None
+    if args.project:
+        # seeded poses near the identity and inverse depths of the step's keyframes
+        prng = np.random.default_rng(configs.SEED + 13)
+        poses_p = torch.from_numpy(configs.random_poses(wl.frames, prng, trans=0.15, angle=0.08)).to(dev)
+        disps_p = torch.from_numpy(prng.uniform(0.15, 1.2, (wl.frames, wl.h, wl.w))
+                                   .astype(np.float32)).to(dev)
+        intr_p = torch.tensor([0.95 * wl.w, 0.95 * wl.w, wl.w / 2 - 0.5, wl.h / 2 - 0.5],
+                              dtype=torch.float32, device=dev)
+        proj = (poses_p, disps_p, intr_p, torch.empty_like(coords),
+                torch.empty(M, wl.h, wl.w, device=dev))
 
     def corr(ii_=None, jj_=None, coords_=None, record=False):
         ii_ = ii_d if ii_ is None else ii_
@@ -250,6 +264,9 @@ def main():
             if evs:
                 evs[2].record(stream)
                 stage_ev.append(evs)
+        elif proj is not None:
+            dc.project_build_and_lookup(proj[0], proj[1], proj[2], ii_, jj_, out=out,
+                                        coords=proj[3], valid=proj[4])
         else:
             dc.build_and_lookup(ii_, jj_, coords_, out)
 
@@ -408,7 +425,9 @@ def main():
         "config": {"workload": f"{wl.name}: {wl.frames} kf {wl.h}x{wl.w}x{wl.channels}, "
                                f"{M} edges per GPU ({wl.mode} workload), build+pyramid+r3 "
                                + ("lookup, volumes materialised in HBM" if vols is not None
-                                  else "lookup, no volume stored"),
+                                  else "lookup, no volume stored")
+                               + (", coords reprojected from poses + inverse depths in the step"
+                                  if proj is not None else ""),
                    "alpha": wl.alpha, "l2": "flushed between steps (252 MB read)",
                    "parallelism": f"edges sharded, dp{world}"},
         "gpu_launches": launches,

@@ -17,6 +17,10 @@
  *   CudaDroid::batch_build_and_sample_correlation          dc_build_and_lookup
  *                                     main.cu:1555-1613
  *   (no reference counterpart: on-the-fly lookup)          dc_alt_lookup
+ *   projmap_kernel                    se3.cuh:118-177      dc_project
+ *   + batch_coords_hw2_to_2hw         main.cu:1135-1146
+ *   projmap + hw2_to_2hw + batch_build_and_sample_...      dc_project_build_and_lookup
+ *                                     main.cu:2188-2201
  *   cuda_pipeline/slam.cuh:2796, :2825, :2851              the same three entry points
  *
  * Conventions (all entry points):
@@ -157,6 +161,37 @@ int dc_build_and_lookup(dc_ctx* ctx, const int* ii_dev, const int* jj_dev, int M
  * materialises, main.cu:2185-2201). */
 int dc_alt_lookup(dc_ctx* ctx, const int* ii_dev, const int* jj_dev, int M,
                   const float* coords_dev, float* out_dev, dc_stream_t stream);
+
+/* Reprojection of every source pixel of edge e into frame jj[e]
+ * (projmap_kernel, se3.cuh:118-177, followed by the layout pass
+ * batch_coords_hw2_to_2hw, main.cu:1135-1146, as one kernel):
+ *   poses_dev      [num_frames][7]   t_x t_y t_z q_x q_y q_z q_w (world -> camera)
+ *   disps_dev      [num_frames][h][w] inverse depth
+ *   intrinsics_dev [4]               fx fy cx cy (at the feature-map resolution)
+ *   coords_dev     [M][2][h][w]      written: x then y, the layout dc_lookup and
+ *                                    dc_build_and_lookup read
+ *   valid_dev      [M][h][w] or NULL written: 1 where the projected depth
+ *                                    exceeds 0.25 (MIN_DEPTH), else 0
+ * Pixels whose projected depth is at most 0.01, and all pixels of an edge whose
+ * ii/jj lies outside [0, num_frames), keep their own coordinates (u, v).
+ * Coordinates agree with the reference kernel to a few float ulps: the
+ * reference is built with --use_fast_math (approximate division). */
+int dc_project(dc_ctx* ctx, const float* poses_dev, const float* disps_dev,
+               const float* intrinsics_dev, int num_frames, const int* ii_dev,
+               const int* jj_dev, int M, float* coords_dev, float* valid_dev,
+               dc_stream_t stream);
+
+/* dc_project followed by dc_build_and_lookup on the projected coordinates: the
+ * reference's per-batch steps 1-3 (main.cu:2188-2201: projmap_kernel, the
+ * layout pass and batch_build_and_sample_correlation) in two kernels, with no
+ * interleaved coordinate buffer.  coords_dev [M][2][h][w] receives the
+ * coordinates (the motion features downstream need them, main.cu:2206-2211);
+ * valid_dev may be NULL. */
+int dc_project_build_and_lookup(dc_ctx* ctx, const float* poses_dev, const float* disps_dev,
+                                const float* intrinsics_dev, int num_frames,
+                                const int* ii_dev, const int* jj_dev, int M,
+                                float* coords_dev, float* valid_dev, float* out_dev,
+                                dc_stream_t stream);
 
 /* Wait for `stream`, then report and clear the device error word that the
  * library's bounded device-side waits raise when they time out: DC_OK or

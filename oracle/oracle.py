@@ -173,3 +173,57 @@ def cpu_build_and_sample(fmaps: np.ndarray, ii: np.ndarray, jj: np.ndarray,
 
 def max_threads() -> int:
     return int(lib().orc_max_threads())
+
+
+# ---------------------------------------------------------------- reprojection
+
+def _rotate(q: np.ndarray, X: np.ndarray) -> np.ndarray:
+    """q X q* in the form of actSO3 (cuda_slam/se3.cuh:8-17): uv = 2 q x X,
+    Y = X + w uv + q x uv.  q = (x, y, z, w); X [..., 3]."""
+    qv, w = q[:3], q[3]
+    uv = 2.0 * np.cross(qv, X)
+    return X + w * uv + np.cross(qv, uv)
+
+
+def relative_pose(pi: np.ndarray, pj: np.ndarray):
+    """G_ij = G_j G_i^-1 for poses (t, q) [7] (relSE3, cuda_slam/se3.cuh:44-55)."""
+    ti, qi, tj, qj = pi[:3], pi[3:], pj[:3], pj[3:]
+    qij = np.array([
+        -qj[3] * qi[0] + qj[0] * qi[3] - qj[1] * qi[2] + qj[2] * qi[1],
+        -qj[3] * qi[1] + qj[1] * qi[3] - qj[2] * qi[0] + qj[0] * qi[2],
+        -qj[3] * qi[2] + qj[2] * qi[3] - qj[0] * qi[1] + qj[1] * qi[0],
+        qj[3] * qi[3] + qj[0] * qi[0] + qj[1] * qi[1] + qj[2] * qi[2]])
+    tij = tj - _rotate(qij, ti)
+    return tij, qij
+
+
+def project(poses: np.ndarray, disps: np.ndarray, intrinsics: np.ndarray, ii, jj):
+    """float64 restatement of projmap_kernel (cuda_slam/se3.cuh:118-177) with the
+    output in the lookup's layout (batch_coords_hw2_to_2hw, main.cu:1135-1146).
+    poses [N, 7], disps [N, H, W], intrinsics (fx, fy, cx, cy).  Returns
+    (coords [M, 2, H, W], valid [M, H, W]); an edge with ii/jj outside [0, N)
+    keeps the pixel grid and is not valid."""
+    poses = np.asarray(poses, np.float64)
+    disps = np.asarray(disps, np.float64)
+    fx, fy, cx, cy = (float(v) for v in intrinsics)
+    N, H, W = disps.shape
+    v, u = np.meshgrid(np.arange(H, dtype=np.float64), np.arange(W, dtype=np.float64),
+                       indexing="ij")
+    M = len(ii)
+    coords = np.empty((M, 2, H, W))
+    valid = np.zeros((M, H, W))
+    for e, (i, j) in enumerate(zip(ii, jj)):
+        if not (0 <= i < N and 0 <= j < N):
+            coords[e, 0], coords[e, 1] = u, v
+            continue
+        tij, qij = relative_pose(poses[i], poses[j])
+        Xi = np.stack([(u - cx) / fx, (v - cy) / fy, np.ones_like(u)], -1)
+        Xj = _rotate(qij, Xi) + disps[i][..., None] * tij
+        z = Xj[..., 2]
+        front = z > 0.01
+        zs = np.where(front, z, 1.0)
+        coords[e, 0] = np.where(front, fx * (Xj[..., 0] / zs) + cx, u)
+        coords[e, 1] = np.where(front, fy * (Xj[..., 1] / zs) + cy, v)
+        valid[e] = (z > 0.25).astype(np.float64)
+    return coords, valid
+

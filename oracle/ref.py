@@ -36,8 +36,28 @@ def lib():
         L.ref_build_and_sample_fp16.argtypes = [_fp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                                 _ip, _ip, ctypes.c_int, _fp, ctypes.c_float,
                                                 _fp, _fp, ctypes.c_int, _fp]
+        L.ref_project.argtypes = [_fp, _fp, _fp, ctypes.c_int, _ip, _ip, ctypes.c_int,
+                                  ctypes.c_int, ctypes.c_int, _fp, _fp]
         _lib = L
     return _lib
+
+
+def project(poses, disps, intrinsics, ii, jj):
+    """The reference's projmap_kernel + batch_coords_hw2_to_2hw on the GPU
+    (se3.cuh:118-177, main.cu:1135-1146).  Returns (coords [M,2,H,W], valid [M,H,W])."""
+    poses = np.ascontiguousarray(poses, np.float32)
+    disps = np.ascontiguousarray(disps, np.float32)
+    intr = np.ascontiguousarray(intrinsics, np.float32)
+    ii = np.ascontiguousarray(ii, np.int32)
+    jj = np.ascontiguousarray(jj, np.int32)
+    N, H, W = disps.shape
+    M = len(ii)
+    coords = np.empty((M, 2, H, W), np.float32)
+    valid = np.empty((M, H, W), np.float32)
+    rc = lib().ref_project(_f(poses), _f(disps), _f(intr), N, ii.ctypes.data_as(_ip),
+                           jj.ctypes.data_as(_ip), M, H, W, _f(coords), _f(valid))
+    assert rc == 0, rc
+    return coords, valid
 
 
 def _f(a):

@@ -19,6 +19,7 @@
 #include <vector>
 
 #include "ref_kernels.cuh"
+#include "se3.cuh"  // the reference header, included where it lies (-I cuda_slam)
 
 #define RCHK(x)                                                                      \
     do {                                                                             \
@@ -57,7 +58,39 @@ struct DBuf {
 
 extern "C" {
 
-int ref_version(void) { return 1; }
+int ref_version(void) { return 2; }
+
+// projmap_kernel (se3.cuh:118-177) then batch_coords_hw2_to_2hw
+// (main.cu:1135-1146), as the update step launches them (main.cu:2188-2197).
+// poses_h [N][7], disps_h [N][H][W], intr_h [4], ii_h / jj_h [M];
+// coords_h [M][2][H][W], valid_h [M][H][W].
+int ref_project(const float* poses_h, const float* disps_h, const float* intr_h, int N,
+                const int* ii_h, const int* jj_h, int M, int H, int W, float* coords_h,
+                float* valid_h) {
+    const int hw = H * W;
+    DBuf<float> poses, disps, intr, hw2, chw, valid;
+    DBuf<int> ii, jj;
+    RCHK(poses.alloc((size_t)N * 7));
+    RCHK(disps.alloc((size_t)N * hw));
+    RCHK(intr.alloc(4));
+    RCHK(ii.alloc(M));
+    RCHK(jj.alloc(M));
+    RCHK(hw2.alloc((size_t)M * hw * 2));
+    RCHK(chw.alloc((size_t)M * hw * 2));
+    RCHK(valid.alloc((size_t)M * hw));
+    RCHK(cudaMemcpy(poses.p, poses_h, (size_t)N * 7 * 4, cudaMemcpyHostToDevice));
+    RCHK(cudaMemcpy(disps.p, disps_h, (size_t)N * hw * 4, cudaMemcpyHostToDevice));
+    RCHK(cudaMemcpy(intr.p, intr_h, 16, cudaMemcpyHostToDevice));
+    RCHK(cudaMemcpy(ii.p, ii_h, (size_t)M * 4, cudaMemcpyHostToDevice));
+    RCHK(cudaMemcpy(jj.p, jj_h, (size_t)M * 4, cudaMemcpyHostToDevice));
+    projmap_kernel<<<M, 256>>>(poses.p, disps.p, intr.p, ii.p, jj.p, hw2.p, valid.p, M, H, W);
+    RCHK(cudaGetLastError());
+    batch_coords_hw2_to_2hw<<<(M * hw + 255) / 256, 256>>>(hw2.p, chw.p, M, hw);
+    RCHK(cudaGetLastError());
+    RCHK(cudaMemcpy(coords_h, chw.p, (size_t)M * hw * 2 * 4, cudaMemcpyDeviceToHost));
+    RCHK(cudaMemcpy(valid_h, valid.p, (size_t)M * hw * 4, cudaMemcpyDeviceToHost));
+    return 0;
+}
 
 // avg_pool_2x2_kernel (main.cu:1150-1170) over [N][H][W].
 int ref_pool(const float* in_h, float* out_h, long long N, int H, int W) {

@@ -63,6 +63,9 @@ SIGNATURES = {
     "dc_launch_count": (_ll, [_vp]),
     "dc_device_status": (_i, [_vp, _vp]),
     "dc_store_slots": (_i, [_vp, _i, _i, ctypes.POINTER(_vp), ctypes.POINTER(_ll)]),
+    "dc_project": (_i, [_vp, _vp, _vp, _vp, _i, _vp, _vp, _i, _vp, _vp, _vp]),
+    "dc_project_build_and_lookup": (_i, [_vp, _vp, _vp, _vp, _i, _vp, _vp, _i, _vp, _vp, _vp,
+                                         _vp]),
     "dc_build_and_lookup_static": (_i, [ctypes.POINTER(DcConfig), _vp, _i, _i, _vp, _vp, _i,
                                         _vp, _vp, _vp]),
 }

@@ -110,3 +110,14 @@ def make_device_inputs(wl: Workload, device, seed: int = SEED):
         noise = torch.randn(M, 2, wl.h, wl.w, generator=g, device=device) * wl.sigma
     coords = (base + noise).contiguous()
     return fm, ii, jj, coords
+
+
+def random_poses(n: int, rng, trans: float = 0.1, angle: float = 0.05) -> np.ndarray:
+    """Seeded camera poses [n, 7] (t_x t_y t_z q_x q_y q_z q_w, unit q) near the
+    identity, as a keyframe window of a SLAM run would have; float32."""
+    t = rng.normal(0, trans, (n, 3))
+    axis = rng.normal(0, 1, (n, 3))
+    axis /= np.linalg.norm(axis, axis=1, keepdims=True)
+    half = 0.5 * rng.normal(0, angle, (n, 1))
+    q = np.concatenate([axis * np.sin(half), np.cos(half)], 1)
+    return np.concatenate([t, q], 1).astype(np.float32)

@@ -210,6 +210,68 @@ class DroidCorrelation:
         """Fused build + pyramid + lookup (no volume in memory)."""
         return self._edge_call(self.lib.dc_build_and_lookup, ii, jj, coords, out, stream)
 
+    def _project_args(self, poses, disps, intrinsics):
+        self._cuda(poses, torch.float32, "poses")
+        self._cuda(disps, torch.float32, "disps")
+        self._cuda(intrinsics, torch.float32, "intrinsics")
+        N = poses.shape[0]
+        if poses.shape != (N, 7) or disps.shape != (N, self.h, self.w) or intrinsics.numel() != 4:
+            raise ValueError(f"poses must be [N, 7], disps [N, {self.h}, {self.w}], intrinsics [4]")
+        return N
+
+    def project(self, poses: torch.Tensor, disps: torch.Tensor, intrinsics: torch.Tensor, ii, jj,
+                coords: Optional[torch.Tensor] = None, valid: Optional[torch.Tensor] = None,
+                stream: Optional[torch.cuda.Stream] = None):
+        """Reproject every source pixel of each edge into frame jj (projmap_kernel,
+        se3.cuh:118-177, plus the [M][hw][2] -> [M][2][hw] layout pass,
+        main.cu:1135-1146).  Returns (coords [M, 2, h, w], valid [M, h, w])."""
+        N = self._project_args(poses, disps, intrinsics)
+        ii, jj = self._edges(ii, jj)
+        M = ii.numel()
+        if coords is None:
+            coords = torch.empty(M, 2, self.h, self.w, device=self.device)
+        if valid is None:
+            valid = torch.empty(M, self.h, self.w, device=self.device)
+        self._cuda(coords, torch.float32, "coords")
+        self._cuda(valid, torch.float32, "valid")
+        s = _stream(stream)
+        for c0 in range(0, M, self.max_edges):
+            m = min(self.max_edges, M - c0)
+            self._check(self.lib.dc_project(self._ctx, poses.data_ptr(), disps.data_ptr(),
+                                            intrinsics.data_ptr(), N, ii[c0].data_ptr(),
+                                            jj[c0].data_ptr(), m, coords[c0].data_ptr(),
+                                            valid[c0].data_ptr(), s))
+        return coords, valid
+
+    def project_build_and_lookup(self, poses: torch.Tensor, disps: torch.Tensor,
+                                 intrinsics: torch.Tensor, ii, jj,
+                                 out: Optional[torch.Tensor] = None,
+                                 coords: Optional[torch.Tensor] = None,
+                                 valid: Optional[torch.Tensor] = None,
+                                 stream: Optional[torch.cuda.Stream] = None):
+        """Reprojection, then the fused build + pyramid + lookup on those
+        coordinates (the reference's per-batch steps 1-3, main.cu:2188-2201).
+        Returns (out [M, 196, h, w], coords [M, 2, h, w], valid [M, h, w])."""
+        N = self._project_args(poses, disps, intrinsics)
+        ii, jj = self._edges(ii, jj)
+        M = ii.numel()
+        if coords is None:
+            coords = torch.empty(M, 2, self.h, self.w, device=self.device)
+        if valid is None:
+            valid = torch.empty(M, self.h, self.w, device=self.device)
+        if out is None:
+            out = torch.empty(M, self.out_channels, self.h, self.w, device=self.device)
+        for t, n in ((coords, "coords"), (valid, "valid"), (out, "out")):
+            self._cuda(t, torch.float32, n)
+        s = _stream(stream)
+        for c0 in range(0, M, self.max_edges):
+            m = min(self.max_edges, M - c0)
+            self._check(self.lib.dc_project_build_and_lookup(
+                self._ctx, poses.data_ptr(), disps.data_ptr(), intrinsics.data_ptr(), N,
+                ii[c0].data_ptr(), jj[c0].data_ptr(), m, coords[c0].data_ptr(),
+                valid[c0].data_ptr(), out[c0].data_ptr(), s))
+        return out, coords, valid
+
     def alt_lookup(self, ii, jj, coords: torch.Tensor, out: Optional[torch.Tensor] = None,
                    stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
         """On-the-fly lookup from the pooled feature maps."""

@@ -226,6 +226,32 @@ int dc_alt_lookup(dc_ctx* ctx, const int* ii, const int* jj, int M, const float*
     return dc_launch_alt(ctx, ii, jj, M, coords, out, (cudaStream_t)stream);
 }
 
+int dc_project(dc_ctx* ctx, const float* poses, const float* disps, const float* intrinsics,
+               int num_frames, const int* ii, const int* jj, int M, float* coords, float* valid,
+               dc_stream_t stream) {
+    if (!ctx) return DC_ERR_INVALID_ARG;
+    int rc = validate_edges(ctx, ii, jj, M);
+    if (rc) return rc;
+    if (num_frames < 1) return dc_fail(ctx, DC_ERR_INVALID_ARG, "num_frames < 1");
+    if (M == 0) return DC_OK;
+    if (!poses || !disps || !intrinsics || !coords)
+        return dc_fail(ctx, DC_ERR_INVALID_ARG, "NULL pointer");
+    return dc_launch_project(ctx, poses, disps, intrinsics, ii, jj, M, num_frames, coords, valid,
+                             (cudaStream_t)stream);
+}
+
+int dc_project_build_and_lookup(dc_ctx* ctx, const float* poses, const float* disps,
+                                const float* intrinsics, int num_frames, const int* ii,
+                                const int* jj, int M, float* coords, float* valid, float* out,
+                                dc_stream_t stream) {
+    if (!ctx) return DC_ERR_INVALID_ARG;
+    if (M > 0 && !out) return dc_fail(ctx, DC_ERR_INVALID_ARG, "NULL pointer");
+    int rc = dc_project(ctx, poses, disps, intrinsics, num_frames, ii, jj, M, coords, valid,
+                        stream);
+    if (rc) return rc;
+    return dc_build_and_lookup(ctx, ii, jj, M, coords, out, stream);
+}
+
 int dc_device_status(dc_ctx* ctx, dc_stream_t stream) {
     if (!ctx) return DC_ERR_INVALID_ARG;
     if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess)

@@ -134,5 +134,8 @@ bool dc_tc_supported(const dc_ctx* ctx);
 int dc_tc_prepare(dc_ctx* ctx);
 int dc_launch_tc(dc_ctx* ctx, const int* ii, const int* jj, int M, const float* coords,
                  float* out, cudaStream_t s);
+int dc_launch_project(dc_ctx* ctx, const float* poses, const float* disps,
+                      const float* intrinsics, const int* ii, const int* jj, int M,
+                      int num_frames, float* coords, float* valid, cudaStream_t s);
 int dc_launch_alt(dc_ctx* ctx, const int* ii, const int* jj, int M, const float* coords,
                   float* out, cudaStream_t s);

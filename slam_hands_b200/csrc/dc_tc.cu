@@ -19,11 +19,10 @@
 //      epilogue of one chunk overlaps the MMAs of the next);
 //   4. the epilogue drains each chunk in 64-column loads (tcgen05.ld) of eight
 //      8-column strips, every strip 8 consecutive target pixels of one row
-//      starting at a multiple of 8; a lane's window needs, per chunk row, at
-//      most two strips (a 32-bit mask over the chunk's strips).  A window of 8 columns starting at
-//      bx touches only strips bx/8 and bx/8 + 1, so a lane copies a strip it
-//      needs into slot 0 or 1 of its window row with two 16-byte stores -- no
-//      per-tap selection;
+//      starting at a multiple of 8.  A window of 8 columns starting at bx
+//      touches only strips bx/8 and bx/8 + 1 of each of its rows (a 32-bit mask
+//      over the chunk's strips), so a lane copies a strip it needs into slot 0
+//      or 1 of its window row with two 16-byte stores -- no per-tap selection;
 //   5. after the last chunk of a level, forms the (2r+1)^2 bilinear outputs in
 //      the reference's order of accumulation (main.cu:1196-1213), reading window
 //      column x at slot column (bx mod 8) + x, and stores them as

@@ -222,6 +222,25 @@ def test_errors_are_statuses(cuda):
     assert rc == 1 and b"max_edges" in lib.dc_last_error(dc._ctx)
 
 
+@pytest.mark.parametrize("precision", ["fp16", "bf16", "fp32"])
+def test_invalid_slots_give_zero_outputs(cuda, oracle, precision):
+    # edges whose slot index is outside [0, max_frames) produce all-zero outputs
+    # (no out-of-bounds reads, and no window data left over from a valid edge
+    # processed before them on the same SM); valid edges around them are exact
+    h, w = 48, 64
+    dc, fm, _, _, coords = setup(h, w, K=4, precision=precision, M=4, sigma=2.0,
+                                 alpha=1 / math.sqrt(128))
+    ii = np.array([0, -1, 2, 1], dtype=np.int32)
+    jj = np.array([1, 2, 99, 3], dtype=np.int32)
+    out = dc.build_and_lookup(ii, jj, torch.from_numpy(coords).cuda()).cpu().numpy()
+    assert dc.lib.dc_device_status(dc._ctx, None) == 0
+    assert np.all(out[1] == 0.0) and np.all(out[2] == 0.0)
+    good = [0, 3]
+    exp = oracle_alt(oracle, fm, ii[good], jj[good], coords[good], 1 / math.sqrt(128), precision)
+    tol = 1e-4 if precision != "fp32" else TOL_FP32
+    assert normwise(out[good], exp) < tol
+
+
 def test_set_frames_fp16_input(cuda, oracle):
     # reference fmaps are __half (main.cu:677): fp16 input is accepted as is
     h, w = 12, 16
