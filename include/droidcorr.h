@@ -21,6 +21,7 @@
  *   + batch_coords_hw2_to_2hw         main.cu:1135-1146
  *   projmap + hw2_to_2hw + batch_build_and_sample_...      dc_project_build_and_lookup
  *                                     main.cu:2188-2201
+ *   GraphAgg scatter_mean loop        main.cu:2255-2294    dc_scatter_mean
  *   cuda_pipeline/slam.cuh:2796, :2825, :2851              the same three entry points
  *
  * Conventions (all entry points):
@@ -192,6 +193,23 @@ int dc_project_build_and_lookup(dc_ctx* ctx, const float* poses_dev, const float
                                 const int* ii_dev, const int* jj_dev, int M,
                                 float* coords_dev, float* valid_dev, float* out_dev,
                                 dc_stream_t stream);
+
+/* GraphAgg scatter-mean (main.cu:2255-2294): for every keyframe k that is the
+ * source of some edge, agg[k'] = mean over edges e with ii[e] == k of feats[e],
+ * k' = k's rank among those keyframes in ascending id order (the reference's
+ * std::set).  One kernel replaces the reference's memset + one scale_add_kernel
+ * launch per edge + one per keyframe, and reproduces its floats bit for bit: a
+ * running fp32 sum from 0 in edge order, then x + (1/n - 1) x as one fused
+ * multiply-add for keyframes with n > 1 edges.
+ *   feats_dev    [E][F]   per-edge features (F = 128*h*w in the reference)
+ *   ii_host      [E]      HOST array of source keyframes (state.ii_host)
+ *   agg_dev      [K][F]   written, K = number of distinct ii (<= E)
+ *   kf_ids_host  [>= K] or NULL: receives the keyframe id of each agg row
+ *   K_out        or NULL: receives K
+ * E <= max_edges.  The edge lists are copied from the host on `stream`
+ * (pageable memory: the call returns once the host data is staged). */
+int dc_scatter_mean(dc_ctx* ctx, const float* feats_dev, long long F, const int* ii_host, int E,
+                    float* agg_dev, int* kf_ids_host, int* K_out, dc_stream_t stream);
 
 /* Wait for `stream`, then report and clear the device error word that the
  * library's bounded device-side waits raise when they time out: DC_OK or

@@ -305,3 +305,44 @@ int orc_cpu_build_and_sample(const float* fmaps, int C, int h, int w, const int*
     }
     return 0;
 }
+
+/* GraphAgg scatter_mean (cuda_slam/main.cu:2255-2294) as the reference runs it:
+ * compact keyframe index = rank of ii[e] among the distinct ii in ascending
+ * order (std::set); the compact buffer starts at 0 (cudaMemset, :2269); every
+ * edge e in order adds its features with scale_add_kernel(dst, src, 1.0f)
+ * (nn.cuh:382-385: dst += scale * src, contracted by nvcc to fmaf(scale, src,
+ * dst)); then keyframes with count > 1 get scale_add_kernel(dst, dst,
+ * 1.0f / count - 1.0f) (:2287-2294), i.e. fmaf(s, dst, dst).
+ * feats [E][F] -> agg [K][F]; ids [K]; returns K. */
+int orc_scatter_mean(const float* feats, long long F, const int* ii, int E, float* agg, int* ids) {
+    int K = 0;
+    for (int e = 0; e < E; e++) {  /* distinct ids, ascending (insertion sort) */
+        int v = ii[e], pos = 0, dup = 0;
+        while (pos < K && ids[pos] < v) pos++;
+        if (pos < K && ids[pos] == v) dup = 1;
+        if (!dup) {
+            for (int m = K; m > pos; m--) ids[m] = ids[m - 1];
+            ids[pos] = v;
+            K++;
+        }
+    }
+    for (long long i = 0; i < (long long)K * F; i++) agg[i] = 0.0f;
+    int* count = (int*)calloc(K > 0 ? K : 1, sizeof(int));
+    for (int e = 0; e < E; e++) {
+        int k = 0;
+        while (ids[k] != ii[e]) k++;
+        float* dst = agg + (size_t)k * F;
+        const float* src = feats + (size_t)e * F;
+        for (long long i = 0; i < F; i++) dst[i] = fmaf(1.0f, src[i], dst[i]);
+        count[k]++;
+    }
+    for (int k = 0; k < K; k++) {
+        if (count[k] > 1) {
+            float s = 1.0f / (float)count[k] - 1.0f;
+            float* dst = agg + (size_t)k * F;
+            for (long long i = 0; i < F; i++) dst[i] = fmaf(s, dst[i], dst[i]);
+        }
+    }
+    free(count);
+    return K;
+}

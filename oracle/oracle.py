@@ -52,6 +52,8 @@ def lib() -> ctypes.CDLL:
         L.orc_cpu_build_and_sample.argtypes = [_fp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                                _ip, _ip, ctypes.c_int, _fp, _fp, ctypes.c_int,
                                                ctypes.c_int, ctypes.c_float, _fp, ctypes.c_int]
+        L.orc_scatter_mean.argtypes = [_fp, ctypes.c_longlong, _ip, ctypes.c_int, _fp, _ip]
+        L.orc_scatter_mean.restype = ctypes.c_int
         _lib = L
     return _lib
 
@@ -227,3 +229,16 @@ def project(poses: np.ndarray, disps: np.ndarray, intrinsics: np.ndarray, ii, jj
         valid[e] = (z > 0.25).astype(np.float64)
     return coords, valid
 
+
+
+def scatter_mean(feats: np.ndarray, ii) -> tuple:
+    """GraphAgg scatter_mean as the reference computes it (orc_scatter_mean,
+    cuda_slam/main.cu:2255-2294).  feats [E, ...] float32 -> (agg [K, ...], ids [K])."""
+    feats = np.ascontiguousarray(feats, np.float32)
+    ii = np.ascontiguousarray(ii, np.int32)
+    E = feats.shape[0]
+    F = int(np.prod(feats.shape[1:]))
+    agg = np.empty((E, F), np.float32)
+    ids = np.empty(E, np.int32)
+    K = lib().orc_scatter_mean(_f(feats), F, _i(ii), E, _f(agg), _i(ids))
+    return agg[:K].reshape((K,) + feats.shape[1:]), ids[:K].copy()

@@ -272,6 +272,30 @@ class DroidCorrelation:
                 valid[c0].data_ptr(), out[c0].data_ptr(), s))
         return out, coords, valid
 
+    def scatter_mean(self, feats: torch.Tensor, ii, agg: Optional[torch.Tensor] = None,
+                     stream: Optional[torch.cuda.Stream] = None):
+        """GraphAgg scatter-mean (main.cu:2255-2294): the mean of feats[e] over the
+        edges e of each distinct source keyframe ii[e], keyframes in ascending id
+        order.  feats [E, ...] float32 on the device, ii a host sequence of E ids.
+        Returns (agg [K, ...], kf_ids np.int32 [K])."""
+        import numpy as np
+
+        self._cuda(feats, torch.float32, "feats")
+        ii_h = np.ascontiguousarray(np.asarray(ii, dtype=np.int32))
+        E = feats.shape[0]
+        if ii_h.shape != (E,):
+            raise ValueError("ii must hold one keyframe id per row of feats")
+        F = feats[0].numel() if E else 0
+        if agg is None:
+            agg = torch.empty((len(np.unique(ii_h)),) + tuple(feats.shape[1:]), device=self.device)
+        self._cuda(agg, torch.float32, "agg")
+        ids = np.empty(max(E, 1), np.int32)
+        K = ctypes.c_int(0)
+        self._check(self.lib.dc_scatter_mean(self._ctx, feats.data_ptr(), F,
+                                             ii_h.ctypes.data, E, agg.data_ptr(),
+                                             ids.ctypes.data, ctypes.byref(K), _stream(stream)))
+        return agg[:K.value], ids[:K.value].copy()
+
     def alt_lookup(self, ii, jj, coords: torch.Tensor, out: Optional[torch.Tensor] = None,
                    stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
         """On-the-fly lookup from the pooled feature maps."""

@@ -6,9 +6,9 @@
 // its window.  One warp owns one (pixel, level) at a time: lane k holds channels
 // [k*CPL, (k+1)*CPL) of f_ii[:, p] in registers, reads the same channels of each
 // tap's target vector (one coalesced C-element row of the pixel-major store) and
-// keeps 64 per-tap partial sums.  A transposed butterfly then reduces the 64
-// partials across the 32 lanes in 62 shuffles (instead of 64 x 5), leaving tap
-// 2k and 2k+1 in lane k.  The bilinear combination uses the reference's rounding
+// keeps per-tap partial sums for 32 taps at a time (the window's two halves).
+// A transposed butterfly then reduces the 32 partials across the 32 lanes in 31
+// shuffles (instead of 32 x 5), leaving tap k in lane k.  The bilinear combination uses the reference's rounding
 // order (batch_corr_sample_kernel, cuda_slam/main.cu:1196-1213).
 //
 // A CTA owns one edge and 32 consecutive source pixels; its 8 warps take 4
@@ -42,12 +42,13 @@ __device__ __forceinline__ void load_ch(const T* p, float (&v)[CPL]) {
     }
 }
 
-// Transposed butterfly: on entry each lane has 64 partial sums x[0..63] (one per
-// tap); on exit lane k holds the full sums of taps 2k (x[0]) and 2k+1 (x[1]).
-__device__ __forceinline__ void reduce64(float (&x)[64], int lane) {
+// Transposed butterfly: on entry each lane has 32 partial sums x[0..31] (one per
+// tap); on exit lane k holds the full sum of tap k in x[0] (31 shuffles instead
+// of 32 x 5).
+__device__ __forceinline__ void reduce32(float (&x)[32], int lane) {
 #pragma unroll
     for (int step = 0; step < 5; step++) {
-        const int half = 32 >> step;  // live entries after this step
+        const int half = 16 >> step;  // live entries after this step
         const int bit = 16 >> step;   // partner distance
         const bool upper = (lane & bit) != 0;
 #pragma unroll
@@ -91,26 +92,31 @@ __global__ void __launch_bounds__(kWarps * 32) alt_lookup_kernel(
             const float dx = x0 - fx, dy = y0 - fy;
             const int bx = (int)fx - R, by = (int)fy - R;
             const T* tgt = store + ((size_t)sj * g.frame_rows + g.row0[l]) * C + lane * CPL;
-            float part[64];
+            // the 8x8 window in two halves of 32 taps (x offsets 0-3, then 4-7):
+            // half the live partial sums, twice the resident warps
 #pragma unroll
-            for (int k = 0; k < 64; k++) {
-                const int i = k >> 3, j = k & 7;  // x offset i, y offset j
-                part[k] = 0.0f;
-                if (i < NW && j < NW && ok) {
-                    const int x1 = bx + i, y1 = by + j;
-                    if ((unsigned)x1 < (unsigned)Wl && (unsigned)y1 < (unsigned)Hl) {
-                        float b[CPL];
-                        load_ch<T, CPL>(tgt + (size_t)(y1 * Wl + x1) * C, b);
-                        float s = 0.0f;
+            for (int hf = 0; hf < 2; hf++) {
+                float part[32];
 #pragma unroll
-                        for (int c = 0; c < CPL; c++) s = fmaf(a[c], b[c], s);
-                        part[k] = s;
+                for (int kk = 0; kk < 32; kk++) {
+                    const int k = 32 * hf + kk;
+                    const int i = k >> 3, j = k & 7;  // x offset i, y offset j
+                    part[kk] = 0.0f;
+                    if (i < NW && j < NW && ok) {
+                        const int x1 = bx + i, y1 = by + j;
+                        if ((unsigned)x1 < (unsigned)Wl && (unsigned)y1 < (unsigned)Hl) {
+                            float b[CPL];
+                            load_ch<T, CPL>(tgt + (size_t)(y1 * Wl + x1) * C, b);
+                            float s = 0.0f;
+#pragma unroll
+                            for (int c = 0; c < CPL; c++) s = fmaf(a[c], b[c], s);
+                            part[kk] = s;
+                        }
                     }
                 }
+                reduce32(part, lane);
+                win[32 * hf + lane] = g.alpha * part[0];
             }
-            reduce64(part, lane);
-            win[2 * lane] = g.alpha * part[0];
-            win[2 * lane + 1] = g.alpha * part[1];
             __syncwarp();
             const float ux = 1.0f - dx, uy = 1.0f - dy;
             for (int o = lane; o < D * D; o += 32) {

@@ -105,7 +105,10 @@ int dc_create(const dc_config* cfg, dc_ctx** out) {
         delete ctx;
         return DC_ERR_CUDA;
     }
-    if (cudaMalloc(&ctx->dev_err, sizeof(int)) != cudaSuccess ||
+    // one small allocation: the device error word, then the scatter-mean lists
+    // (dc_scatter_mean: edge order, list offsets and mean scales, max_edges each)
+    const size_t small_words = 32 + 3 * (size_t)c.max_edges + 1;
+    if (cudaMalloc(&ctx->dev_err, small_words * sizeof(int)) != cudaSuccess ||
         cudaMemset(ctx->dev_err, 0, sizeof(int)) != cudaSuccess) {
         cudaFree(ctx->store);
         delete ctx;
@@ -250,6 +253,21 @@ int dc_project_build_and_lookup(dc_ctx* ctx, const float* poses, const float* di
                         stream);
     if (rc) return rc;
     return dc_build_and_lookup(ctx, ii, jj, M, coords, out, stream);
+}
+
+int dc_scatter_mean(dc_ctx* ctx, const float* feats, long long F, const int* ii_host, int E,
+                    float* agg, int* kf_ids_host, int* K_out, dc_stream_t stream) {
+    if (!ctx) return DC_ERR_INVALID_ARG;
+    if (K_out) *K_out = 0;
+    if (E < 0 || E > ctx->cfg.max_edges)
+        return dc_fail(ctx, DC_ERR_INVALID_ARG,
+                       "E=" + std::to_string(E) + " outside [0, max_edges=" +
+                           std::to_string(ctx->cfg.max_edges) + "]");
+    if (F < 1) return dc_fail(ctx, DC_ERR_INVALID_ARG, "F < 1");
+    if (E == 0) return DC_OK;
+    if (!feats || !ii_host || !agg) return dc_fail(ctx, DC_ERR_INVALID_ARG, "NULL pointer");
+    return dc_scatter_mean_impl(ctx, feats, F, ii_host, E, agg, kf_ids_host, K_out,
+                                (cudaStream_t)stream);
 }
 
 int dc_device_status(dc_ctx* ctx, dc_stream_t stream) {

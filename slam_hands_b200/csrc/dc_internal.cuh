@@ -34,7 +34,8 @@ struct dc_ctx {
     long long store_bytes = 0;
     int num_sms = 148;
     long long launches = 0;
-    int* dev_err = nullptr;  // device error word raised by bounded device waits
+    int* dev_err = nullptr;  // device error word raised by bounded device waits; the same
+                             // allocation holds the scatter-mean lists from word 32 on
     // tensor map of the store for the tensor-core kernel (CUtensorMap storage)
     alignas(64) unsigned char tmap_a[128];
     // per level, a 4-D map [slot][H_l][W_l][C] of the same store with boxes of
@@ -137,5 +138,7 @@ int dc_launch_tc(dc_ctx* ctx, const int* ii, const int* jj, int M, const float* 
 int dc_launch_project(dc_ctx* ctx, const float* poses, const float* disps,
                       const float* intrinsics, const int* ii, const int* jj, int M,
                       int num_frames, float* coords, float* valid, cudaStream_t s);
+int dc_scatter_mean_impl(dc_ctx* ctx, const float* feats, long long F, const int* ii_host,
+                         int E, float* agg, int* kf_ids_host, int* K_out, cudaStream_t s);
 int dc_launch_alt(dc_ctx* ctx, const int* ii, const int* jj, int M, const float* coords,
                   float* out, cudaStream_t s);

@@ -1,0 +1,42 @@
+"""GraphAgg scatter-mean (dc_scatter_mean, main.cu:2255-2294).
+
+CPU: the oracle (orc_scatter_mean, the reference's memset + per-edge
+scale_add_kernel + per-keyframe scale loop) against plain numpy means.
+GPU: the library's one-kernel version against the oracle, bit for bit."""
+import numpy as np
+import pytest
+import torch
+
+from slam_hands_b200 import DroidCorrError, DroidCorrelation
+
+
+def test_oracle_is_the_mean_in_ascending_keyframe_order(oracle):
+    rng = np.random.default_rng(0)
+    feats = rng.standard_normal((9, 4, 5, 6), dtype=np.float32)
+    ii = np.array([4, 1, 4, 9, 1, 4, 2, 9, 4], np.int32)
+    agg, ids = oracle.scatter_mean(feats, ii)
+    assert list(ids) == [1, 2, 4, 9]
+    for k, kf in enumerate(ids):
+        exp = feats[ii == kf].astype(np.float64).mean(0)
+        assert np.abs(agg[k] - exp).max() < 1e-6
+    assert np.array_equal(agg[1], feats[6])  # one edge: copied exactly
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("E,shape", [(48, (128, 48, 64)), (13, (3, 7, 9)), (1, (128, 12, 16))])
+def test_scatter_mean_bit_exact_vs_oracle(cuda, oracle, E, shape):
+    rng = np.random.default_rng(E)
+    feats = rng.standard_normal((E,) + shape, dtype=np.float32)
+    ii = rng.integers(0, max(2, E // 3), E).astype(np.int32)
+    dc = DroidCorrelation(12, 16, max_frames=4, max_edges=64)
+    agg, ids = dc.scatter_mean(torch.from_numpy(feats).cuda(), ii)
+    exp, exp_ids = oracle.scatter_mean(feats, ii)
+    assert np.array_equal(ids, exp_ids)
+    assert np.array_equal(agg.cpu().numpy(), exp)
+
+
+@pytest.mark.gpu
+def test_scatter_mean_rejects_too_many_edges(cuda):
+    dc = DroidCorrelation(12, 16, max_frames=4, max_edges=4)
+    with pytest.raises(DroidCorrError):
+        dc.scatter_mean(torch.zeros(5, 8, device="cuda"), [0, 1, 2, 3, 0])
