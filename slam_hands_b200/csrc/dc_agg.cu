@@ -38,13 +38,24 @@ __global__ void __launch_bounds__(kAggThreads) scatter_mean_kernel(
         const long long i = (long long)blockIdx.x * kAggThreads + threadIdx.x;  // float4 index
         if (i >= F / 4) return;
         float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        for (int t = e0; t < e1; t++) {
-            const float4 v = __ldcs(reinterpret_cast<const float4*>(feats + (size_t)order[t] * F) + i);
+        auto add = [&](const float4& v) {
             acc.x = __fadd_rn(acc.x, v.x);
             acc.y = __fadd_rn(acc.y, v.y);
             acc.z = __fadd_rn(acc.z, v.z);
             acc.w = __fadd_rn(acc.w, v.w);
+        };
+        auto load = [&](int t) {
+            return __ldcs(reinterpret_cast<const float4*>(feats + (size_t)order[t] * F) + i);
+        };
+        int t = e0;
+        for (; t + 4 <= e1; t += 4) {  // four loads in flight, added in edge order
+            const float4 v0 = load(t), v1 = load(t + 1), v2 = load(t + 2), v3 = load(t + 3);
+            add(v0);
+            add(v1);
+            add(v2);
+            add(v3);
         }
+        for (; t < e1; t++) add(load(t));
         if (e1 - e0 > 1) {
             acc.x = fmaf(sc, acc.x, acc.x);
             acc.y = fmaf(sc, acc.y, acc.y);
