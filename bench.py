@@ -345,18 +345,70 @@ def main():
         corr(ii_d2, jj_d2, coords_d2)
         out_h.copy_(out, non_blocking=True)
 
-    for _ in range(3):
-        e2e_step()
+    # Pipelined end to end (fused path): step k's input copies, its correlation
+    # in E2E_CHUNKS edge chunks, and each chunk's output copy run on three
+    # streams, so the host->device copy of step k+1 and the compute of later
+    # chunks overlap the device->host copy of earlier outputs (PCIe is full
+    # duplex).  Inputs and outputs are double-buffered by step parity.
+    pipelined = vols is None and proj is None
+    E2E_CHUNKS = 4
+    if pipelined:
+        s_h2d, s_comp, s_d2h = (torch.cuda.Stream(dev) for _ in range(3))
+        bufs = [dict(fm=torch.empty_like(fm), coords=torch.empty_like(coords),
+                     ii=torch.empty_like(ii_d), jj=torch.empty_like(jj_d),
+                     out=torch.empty_like(out)) for _ in range(2)]
+        bounds = [(M * c // E2E_CHUNKS, M * (c + 1) // E2E_CHUNKS) for c in range(E2E_CHUNKS)]
+        bounds = [(a, b) for a, b in bounds if b > a]
+        ev_in = [torch.cuda.Event() for _ in range(2)]
+        ev_used = [torch.cuda.Event() for _ in range(2)]
+        ev_free = [torch.cuda.Event() for _ in range(2)]
+        ev_chunk = [[torch.cuda.Event() for _ in bounds] for _ in range(2)]
+
+        def e2e_pipe_step(k):
+            b, B = k % 2, bufs[k % 2]
+            with torch.cuda.stream(s_h2d):
+                if k >= 2:
+                    s_h2d.wait_event(ev_used[b])  # compute of step k-2 is done with them
+                if rank == 0:
+                    B["fm"].copy_(fm_h, non_blocking=True)
+                B["coords"].copy_(coords_h, non_blocking=True)
+                B["ii"].copy_(ii_h, non_blocking=True)
+                B["jj"].copy_(jj_h, non_blocking=True)
+                ev_in[b].record(s_h2d)
+            with torch.cuda.stream(s_comp):
+                s_comp.wait_event(ev_in[b])
+                if k >= 2:
+                    s_comp.wait_event(ev_free[b])  # the output copy of step k-2 is done
+                if rank == 0:
+                    dc.set_frames(B["fm"], stream=s_comp)
+                if pg is not None:
+                    replicate_store(dc, 0, wl.frames)
+                for c, (a0, a1) in enumerate(bounds):
+                    dc.build_and_lookup(B["ii"][a0:a1], B["jj"][a0:a1], B["coords"][a0:a1],
+                                        out=B["out"][a0:a1], stream=s_comp)
+                    ev_chunk[b][c].record(s_comp)
+                ev_used[b].record(s_comp)
+            with torch.cuda.stream(s_d2h):
+                for c, (a0, a1) in enumerate(bounds):
+                    s_d2h.wait_event(ev_chunk[b][c])
+                    out_h[a0:a1].copy_(B["out"][a0:a1], non_blocking=True)
+                ev_free[b].record(s_d2h)
+
+    for k in range(3):
+        e2e_pipe_step(k) if pipelined else e2e_step()
     torch.cuda.synchronize()
     if pg is not None:
         pg.barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    torch.cuda._sleep(int(0.02 * 1.9e9))
-    e0.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
-    e1.record(stream)
+    first = s_h2d if pipelined else stream
+    last = s_d2h if pipelined else stream
+    with torch.cuda.stream(first):
+        torch.cuda._sleep(int(0.02 * 1.9e9))
+    e0.record(first)
+    for k in range(args.steps):
+        e2e_pipe_step(k) if pipelined else e2e_step()
+    e1.record(last)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / args.steps
     if pg is not None:
@@ -370,6 +422,8 @@ def main():
     if rank == 0:
         torch.cuda.synchronize()
         assert torch.isfinite(out).all().item()
+        if pipelined:  # the pipelined host copy holds the same bits as the timed output
+            assert torch.equal(out_h, out.cpu())
 
     if rank != 0:
         if pg is not None:
@@ -437,7 +491,9 @@ def main():
                      "kernel": kernel_name, "peak_source": peak_src,
                      "alg_bytes_per_launch": alg_bytes},
         "e2e": {"value": M * world / (e2e_ms * 1e-3), "unit": UNIT,
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+                "pipelined": (f"{E2E_CHUNKS} edge chunks; input copy, compute and output copy "
+                              "on three streams, double-buffered" if pipelined else False)},
         "clocks": clk,
     }
     if stages is not None:
