@@ -49,6 +49,8 @@ def parse():
     ap.add_argument("--precision", default="fp16", choices=["fp32", "tf32", "bf16", "fp16"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-gpu", action="store_true")
+    ap.add_argument("--scatter-mean", action="store_true",
+                    help="time dc_scatter_mean (GraphAgg) at the workload's sizes instead")
     ap.add_argument("--project", action="store_true",
                     help="coordinates from poses + inverse depths inside the step "
                          "(dc_project_build_and_lookup: reprojection + fused correlation)")
@@ -184,6 +186,41 @@ def run_reference_arm(args, wl):
 
 # ---------------------------------------------------------------- GPU arm
 
+def run_scatter_mean(args, wl):
+    """GraphAgg scatter-mean at the workload's sizes (one GPU): E = the batch's
+    edges, F = 128 * h * w features per edge, keyframe ids = the batch's ii.
+    Prints one JSON line with CUDA-event times (median of `steps`) of the whole
+    dc_scatter_mean call and HBM GB/s on its algorithmic bytes."""
+    from slam_hands_b200 import DroidCorrelation, configs
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    ii, _ = configs.make_edges(wl, seed=configs.SEED)
+    ii = np.asarray(ii, np.int32)
+    E, F = len(ii), 128 * wl.h * wl.w
+    K = len(np.unique(ii))
+    feats = torch.randn(E, F, device=dev)
+    dc = DroidCorrelation(wl.h, wl.w, max_frames=wl.frames, max_edges=E, device=dev)
+    agg = torch.empty(K, F, device=dev)
+    flush = torch.empty(2 * L2_BYTES // 4, device=dev)
+    for _ in range(max(args.warmup, 3)):
+        dc.scatter_mean(feats, ii, agg=agg)
+    ts = []
+    for _ in range(args.steps):
+        flush.add_(1.0)  # L2 flush between calls
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        dc.scatter_mean(feats, ii, agg=agg)
+        b.record()
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b))
+    ms = statistics.median(ts)
+    byts = (E + K) * F * 4
+    print(json.dumps({"kernel": "dc_scatter_mean", "workload": wl.name, "E": E, "K": K, "F": F,
+                      "ms_per_call": ms, "alg_bytes": byts, "GBs": byts / (ms * 1e-3) / 1e9}))
+    return 0
+
+
 def main():
     args = parse()
     from slam_hands_b200 import configs
@@ -191,6 +228,8 @@ def main():
     wl = configs.WORKLOADS[args.workload]
     if args.impl == "reference":
         return run_reference_arm(args, wl)
+    if args.scatter_mean:
+        return run_scatter_mean(args, wl)
 
     from slam_hands_b200 import DroidCorrelation
     from slam_hands_b200.shard import edge_range, replicate_store
