@@ -22,6 +22,7 @@
  *   projmap + hw2_to_2hw + batch_build_and_sample_...      dc_project_build_and_lookup
  *                                     main.cu:2188-2201
  *   GraphAgg scatter_mean loop        main.cu:2255-2294    dc_scatter_mean
+ *   per-edge inps[ii[e]] copy loop    main.cu:2215-2224    dc_gather_rows
  *   cuda_pipeline/slam.cuh:2796, :2825, :2851              the same three entry points
  *
  * Conventions (all entry points):
@@ -210,6 +211,16 @@ int dc_project_build_and_lookup(dc_ctx* ctx, const float* poses_dev, const float
  * (pageable memory: the call returns once the host data is staged). */
 int dc_scatter_mean(dc_ctx* ctx, const float* feats_dev, long long F, const int* ii_host, int E,
                     float* agg_dev, int* kf_ids_host, int* K_out, dc_stream_t stream);
+
+/* Row gather for the update step's per-edge loads (main.cu:2215-2224, one
+ * synchronous cudaMemcpy per edge: batch_inps[e] = inps[ii[bs + e]]):
+ * dst_dev[e] = src_dev[idx_dev[e]] for e < n, rows of F floats, one launch on
+ * `stream`.  src_dev [num_rows][F], idx_dev [n] (device), dst_dev [n][F].
+ * Rows whose index is outside [0, num_rows) are written as zeros.  n <= 65535.
+ * (The loop's contiguous copies, edge_nets <-> batch_nets and batch_agg1 ->
+ * all_agg1, are single ranges: one cudaMemcpyAsync each.) */
+int dc_gather_rows(dc_ctx* ctx, const float* src_dev, long long F, int num_rows,
+                   const int* idx_dev, int n, float* dst_dev, dc_stream_t stream);
 
 /* Wait for `stream`, then report and clear the device error word that the
  * library's bounded device-side waits raise when they time out: DC_OK or

@@ -67,6 +67,7 @@ SIGNATURES = {
     "dc_project_build_and_lookup": (_i, [_vp, _vp, _vp, _vp, _i, _vp, _vp, _i, _vp, _vp, _vp,
                                          _vp]),
     "dc_scatter_mean": (_i, [_vp, _vp, _ll, _vp, _i, _vp, _vp, _vp, _vp]),
+    "dc_gather_rows": (_i, [_vp, _vp, _ll, _i, _vp, _i, _vp, _vp]),
     "dc_build_and_lookup_static": (_i, [ctypes.POINTER(DcConfig), _vp, _i, _i, _vp, _vp, _i,
                                         _vp, _vp, _vp]),
 }

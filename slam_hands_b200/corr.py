@@ -296,6 +296,22 @@ class DroidCorrelation:
                                              ids.ctypes.data, ctypes.byref(K), _stream(stream)))
         return agg[:K.value], ids[:K.value].copy()
 
+    def gather_rows(self, src: torch.Tensor, idx, dst: Optional[torch.Tensor] = None,
+                    stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+        """dst[e] = src[idx[e]] (rows = src[0]'s elements) in one launch: the
+        update step's per-edge `inps[ii[e]]` loads (main.cu:2215-2224).
+        Out-of-range indices give zero rows."""
+        self._cuda(src, torch.float32, "src")
+        idx = torch.as_tensor(idx, dtype=torch.int32, device=self.device).contiguous()
+        n = idx.numel()
+        if dst is None:
+            dst = torch.empty((n,) + tuple(src.shape[1:]), device=self.device)
+        self._cuda(dst, torch.float32, "dst")
+        F = src[0].numel()
+        self._check(self.lib.dc_gather_rows(self._ctx, src.data_ptr(), F, src.shape[0],
+                                            idx.data_ptr(), n, dst.data_ptr(), _stream(stream)))
+        return dst
+
     def alt_lookup(self, ii, jj, coords: torch.Tensor, out: Optional[torch.Tensor] = None,
                    stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
         """On-the-fly lookup from the pooled feature maps."""

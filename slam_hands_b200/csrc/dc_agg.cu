@@ -120,3 +120,51 @@ int dc_scatter_mean_impl(dc_ctx* ctx, const float* feats, long long F, const int
     if (K_out) *K_out = K;
     return dc_check_launch(ctx, "scatter_mean_kernel");
 }
+
+// ---- row gather (the update step's per-edge input loads) -------------------
+//
+// Replaces the per-edge cudaMemcpy loop of main.cu:2215-2224 that loads
+// batch_inps[e] = inps[ii[bs + e]] (one synchronous device-to-device copy per
+// edge): dst[e] = src[idx[e]] for rows of F floats, one launch, float4
+// streaming loads and stores.  Rows whose index is outside [0, num_rows) are
+// written as zeros.
+namespace {
+
+template <bool kVec>
+__global__ void __launch_bounds__(kAggThreads) gather_rows_kernel(
+    const float* __restrict__ src, long long F, int num_rows, const int* __restrict__ idx,
+    float* __restrict__ dst) {
+    const int e = blockIdx.y;
+    const int r = __ldg(idx + e);
+    const bool ok = r >= 0 && r < num_rows;
+    const long long stride = (long long)gridDim.x * kAggThreads;
+    if (kVec) {
+        const float4* s = reinterpret_cast<const float4*>(src + (size_t)(ok ? r : 0) * F);
+        float4* d = reinterpret_cast<float4*>(dst + (size_t)e * F);
+        for (long long i = (long long)blockIdx.x * kAggThreads + threadIdx.x; i < F / 4; i += stride)
+            __stcs(d + i, ok ? __ldcs(s + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f));
+    } else {
+        const float* s = src + (size_t)(ok ? r : 0) * F;
+        float* d = dst + (size_t)e * F;
+        for (long long i = (long long)blockIdx.x * kAggThreads + threadIdx.x; i < F; i += stride)
+            d[i] = ok ? __ldcs(s + i) : 0.0f;
+    }
+}
+
+}  // namespace
+
+int dc_gather_rows_impl(dc_ctx* ctx, const float* src, long long F, int num_rows, const int* idx,
+                        int n, float* dst, cudaStream_t s) {
+    const bool vec = (F % 4) == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(dst) & 15) == 0;
+    const long long work = vec ? F / 4 : F;
+    long long bx = (work + kAggThreads * 4 - 1) / (kAggThreads * 4);  // ~4 items per thread
+    if (bx < 1) bx = 1;
+    if (bx > 65535) bx = 65535;
+    dim3 grid((unsigned)bx, n);
+    if (vec)
+        gather_rows_kernel<true><<<grid, kAggThreads, 0, s>>>(src, F, num_rows, idx, dst);
+    else
+        gather_rows_kernel<false><<<grid, kAggThreads, 0, s>>>(src, F, num_rows, idx, dst);
+    return dc_check_launch(ctx, "gather_rows_kernel");
+}

@@ -270,6 +270,16 @@ int dc_scatter_mean(dc_ctx* ctx, const float* feats, long long F, const int* ii_
                                 (cudaStream_t)stream);
 }
 
+int dc_gather_rows(dc_ctx* ctx, const float* src, long long F, int num_rows, const int* idx,
+                   int n, float* dst, dc_stream_t stream) {
+    if (!ctx) return DC_ERR_INVALID_ARG;
+    if (n < 0 || n > 65535) return dc_fail(ctx, DC_ERR_INVALID_ARG, "n outside [0, 65535]");
+    if (F < 1 || num_rows < 1) return dc_fail(ctx, DC_ERR_INVALID_ARG, "F < 1 or num_rows < 1");
+    if (n == 0) return DC_OK;
+    if (!src || !idx || !dst) return dc_fail(ctx, DC_ERR_INVALID_ARG, "NULL pointer");
+    return dc_gather_rows_impl(ctx, src, F, num_rows, idx, n, dst, (cudaStream_t)stream);
+}
+
 int dc_device_status(dc_ctx* ctx, dc_stream_t stream) {
     if (!ctx) return DC_ERR_INVALID_ARG;
     if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess)

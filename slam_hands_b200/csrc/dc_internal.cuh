@@ -140,5 +140,7 @@ int dc_launch_project(dc_ctx* ctx, const float* poses, const float* disps,
                       int num_frames, float* coords, float* valid, cudaStream_t s);
 int dc_scatter_mean_impl(dc_ctx* ctx, const float* feats, long long F, const int* ii_host,
                          int E, float* agg, int* kf_ids_host, int* K_out, cudaStream_t s);
+int dc_gather_rows_impl(dc_ctx* ctx, const float* src, long long F, int num_rows, const int* idx,
+                        int n, float* dst, cudaStream_t s);
 int dc_launch_alt(dc_ctx* ctx, const int* ii, const int* jj, int M, const float* coords,
                   float* out, cudaStream_t s);

@@ -1,4 +1,5 @@
-"""GraphAgg scatter-mean (dc_scatter_mean, main.cu:2255-2294).
+"""GraphAgg scatter-mean (dc_scatter_mean, main.cu:2255-2294) and the update
+step's per-edge row gather (dc_gather_rows, main.cu:2215-2224).
 
 CPU: the oracle (orc_scatter_mean, the reference's memset + per-edge
 scale_add_kernel + per-keyframe scale loop) against plain numpy means.
@@ -40,3 +41,17 @@ def test_scatter_mean_rejects_too_many_edges(cuda):
     dc = DroidCorrelation(12, 16, max_frames=4, max_edges=4)
     with pytest.raises(DroidCorrError):
         dc.scatter_mean(torch.zeros(5, 8, device="cuda"), [0, 1, 2, 3, 0])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("shape", [(128, 48, 64), (5, 7, 3)])
+def test_gather_rows_exact(cuda, shape):
+    # the update step's per-edge inps[ii[e]] loads (main.cu:2215-2224) in one launch
+    rng = np.random.default_rng(7)
+    src = rng.standard_normal((12,) + shape, dtype=np.float32)
+    idx = np.array([3, 0, 11, 3, 7, -1, 12, 5], np.int32)  # two out of range
+    dc = DroidCorrelation(12, 16, max_frames=4, max_edges=8)
+    got = dc.gather_rows(torch.from_numpy(src).cuda(), idx).cpu().numpy()
+    for e, r in enumerate(idx):
+        exp = src[r] if 0 <= r < 12 else np.zeros(shape, np.float32)
+        assert np.array_equal(got[e], exp)
