@@ -493,11 +493,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                         DC_TRACE(0, gc);
                         const LevelBox& B = P.box[lv];
                         const ChunkGeo cg = chunk_geo(sch[lv], B, c - sch[lv].first);
-#if defined(DC_TC_EXP) && (DC_TC_EXP & 8)
-                        mbar_arrive(bar(kBarFull + s));
-                        last_gc = gc + 1;
-                        continue;
-#endif
                         mbar_arrive_expect_tx(bar(kBarFull + s),
                                               P.atoms * B.wbox * B.br * kRowBytes);
                         for (int k = 0; k < P.atoms; k++)
@@ -569,9 +564,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             const uint64_t ad = sdesc_sw128(sA + at * kTileM * kRowBytes + wi * 32);
                             const uint64_t bd = sdesc_sw128(sB + s * Ly.stage_b +
                                                             at * kChunkN * kRowBytes + wi * 32);
-#if !(defined(DC_TC_EXP) && (DC_TC_EXP & 4))
                             mma_f16(d, ad, bd, idesc, kk > 0 ? 1u : 0u);
-#endif
                         }
                         mma_commit(bar(kBarEmpty + s));
                         mma_commit(bar(kBarTFull + a));
@@ -675,21 +668,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if ((unsigned)xs0 < (unsigned)spr) m |= rr << xs0;
                         if ((unsigned)(xs0 + 1) < (unsigned)spr) m |= rr << (xs0 + 1);
                     }
-#if defined(DC_TC_EXP) && (DC_TC_EXP & 1)
-                    const bool need_ld = m != 0;
-                    m = 0;
-#endif
                     // this warp's 64-column blocks: chunk strips 8 * (kWarpBlocks * sub + bb) ..
 #pragma unroll
                     for (int bb = 0; bb < kWarpBlocks; bb++) {
                         const int blk = kWarpBlocks * sub + bb;
                         if (64 * blk >= cg.cols) break;
                         const unsigned n8 = (m >> (8 * blk)) & 0xffu;
-#if defined(DC_TC_EXP) && (DC_TC_EXP & 1)
-                        if (!__any_sync(0xffffffffu, need_ld)) continue;
-#else
                         if (!__any_sync(0xffffffffu, n8 != 0)) continue;
-#endif
                         float v[64];
                         tmem_ld64(tl + (uint32_t)(a * kAccCols + 64 * blk), v);
                         if (lane == 0 && warp == 2) DC_TRACE(5 + bb, gc);
@@ -720,11 +705,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     0xffffffffu, !pv || (any && bx >= 0 && bx + NW - 1 < Wl && by >= 0 &&
                                          by + NW - 1 < Hl));
                 quarter_sync(quarter);  // all strips of this level are in the windows
-#if defined(DC_TC_EXP) && (DC_TC_EXP & 2)
-                if (false) {
-#else
                 if (pv) {
-#endif
                     constexpr int AW = (D + kSubWarps - 1) / kSubWarps;  // 4, 3 at R = 3
                     float* ol = out_e + (size_t)(l * D * D) * hw + p;
                     if (interior_all)
