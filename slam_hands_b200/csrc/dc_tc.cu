@@ -362,7 +362,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         //      coordinates loaded one tile ahead), then the source tile and the
         //      target-row chunks through TMA (one elected lane)
         int gc = 0, na = 0, i = 0;
-        int a_issued = 0, last_gc = 0;
+        int a_issued = 0, a_parity = 0, last_gc = 0;
         float cxn[kTileM / 32], cyn[kTileM / 32];
         int sin_ = -1, sjn = -1;
 #define DC_TC_LOAD_COORDS(tt)                                                      \
@@ -468,38 +468,46 @@ __global__ void __launch_bounds__(kThreads, 1)
             const TileInfo ti = tinfo[tb];
             const LevelSched* sch = sched_base + tb * DC_MAX_LEVELS;
             if (lane == 0 && ti.n > 0) {
-                // the single source-tile buffer: wait until the MMAs of the previous
-                // tile that used it are done
-                if (na >= 1 && !mbar_wait(bar(kBarAEmpty), (na - 1) & 1, abort)) {
-                    raise_abort(abort, P.err, 3);
-                } else {
-                    mbar_arrive_expect_tx(bar(kBarAFull), P.atoms * kTileM * kRowBytes);
-                    const int arow = (int)((long long)ti.si * g.frame_rows + g.row0[0] + ti.p0);
-                    for (int k = 0; k < P.atoms; k++)
-                        tma_load_2d(sA + k * kTileM * kRowBytes, &maps.a, k * 64, arow,
-                                    bar(kBarAFull));
-                    a_issued = 1;
-                    int lv = 0;
-                    for (int c = 0; c < ti.n; c++, gc++) {
-                        while (c >= sch[lv].first + sch[lv].count) lv++;
-                        const int s = gc % kStagesB;
-                        const long long t0 = DC_PROF_NOW();
-                        if (gc >= kStagesB &&
-                            !mbar_wait(bar(kBarEmpty + s), ((gc / kStagesB) - 1) & 1, abort)) {
-                            raise_abort(abort, P.err, 4);
+                // The first kStagesB target-row chunks do not depend on the single
+                // source-tile buffer: issue them first, so their loads overlap the
+                // previous tile's last MMAs; then wait until those MMAs release the
+                // source buffer and load this tile's source pixels.
+                const int pre = min(kStagesB, ti.n);
+                int lv = 0;
+                for (int c = 0; c <= ti.n; c++) {
+                    if (c == pre) {
+                        if (na >= 1 && !mbar_wait(bar(kBarAEmpty), (na - 1) & 1, abort)) {
+                            raise_abort(abort, P.err, 3);
                             break;
                         }
-                        w_a += DC_PROF_NOW() - t0;
-                        DC_TRACE(0, gc);
-                        const LevelBox& B = P.box[lv];
-                        const ChunkGeo cg = chunk_geo(sch[lv], B, c - sch[lv].first);
-                        mbar_arrive_expect_tx(bar(kBarFull + s),
-                                              P.atoms * B.wbox * B.br * kRowBytes);
+                        mbar_arrive_expect_tx(bar(kBarAFull), P.atoms * kTileM * kRowBytes);
+                        const int arow =
+                            (int)((long long)ti.si * g.frame_rows + g.row0[0] + ti.p0);
                         for (int k = 0; k < P.atoms; k++)
-                            tma_load_4d(sB + s * Ly.stage_b + k * kChunkN * kRowBytes, &maps.b[lv],
-                                        k * 64, cg.x0, cg.y0, ti.sj, bar(kBarFull + s));
-                        last_gc = gc + 1;
+                            tma_load_2d(sA + k * kTileM * kRowBytes, &maps.a, k * 64, arow,
+                                        bar(kBarAFull));
+                        a_issued = 1;
+                        a_parity = na & 1;
                     }
+                    if (c == ti.n) break;
+                    while (c >= sch[lv].first + sch[lv].count) lv++;
+                    const int s = gc % kStagesB;
+                    const long long t0 = DC_PROF_NOW();
+                    if (gc >= kStagesB &&
+                        !mbar_wait(bar(kBarEmpty + s), ((gc / kStagesB) - 1) & 1, abort)) {
+                        raise_abort(abort, P.err, 4);
+                        break;
+                    }
+                    w_a += DC_PROF_NOW() - t0;
+                    DC_TRACE(0, gc);
+                    const LevelBox& B = P.box[lv];
+                    const ChunkGeo cg = chunk_geo(sch[lv], B, c - sch[lv].first);
+                    mbar_arrive_expect_tx(bar(kBarFull + s), P.atoms * B.wbox * B.br * kRowBytes);
+                    for (int k = 0; k < P.atoms; k++)
+                        tma_load_4d(sB + s * Ly.stage_b + k * kChunkN * kRowBytes, &maps.b[lv],
+                                    k * 64, cg.x0, cg.y0, ti.sj, bar(kBarFull + s));
+                    gc++;
+                    last_gc = gc;
                 }
             }
             if (ti.n > 0) na++;
@@ -509,7 +517,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             DC_PROF_STORE(4, w_a);
             if (*abort) {
                 // let this CTA's copies in flight land before the CTA exits
-                if (a_issued) mbar_wait(bar(kBarAFull), (na - 1) & 1, nullptr);
+                if (a_issued) mbar_wait(bar(kBarAFull), a_parity, nullptr);
                 for (int c = max(0, last_gc - kStagesB); c < last_gc; c++)
                     mbar_wait(bar(kBarFull + c % kStagesB), (c / kStagesB) & 1, nullptr);
             }
