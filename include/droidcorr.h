@@ -208,7 +208,10 @@ int dc_project_build_and_lookup(dc_ctx* ctx, const float* poses_dev, const float
  *   kf_ids_host  [>= K] or NULL: receives the keyframe id of each agg row
  *   K_out        or NULL: receives K
  * E <= max_edges.  The edge lists are copied from the host on `stream`
- * (pageable memory: the call returns once the host data is staged). */
+ * (pageable memory: the call returns once the host data is staged) into a
+ * small buffer of the context, so two dc_scatter_mean calls on one context
+ * must not overlap on the GPU (use one stream per context, or separate
+ * contexts). */
 int dc_scatter_mean(dc_ctx* ctx, const float* feats_dev, long long F, const int* ii_host, int E,
                     float* agg_dev, int* kf_ids_host, int* K_out, dc_stream_t stream);
 
