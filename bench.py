@@ -504,13 +504,26 @@ def main():
     if stages is not None:
         stages["build_volume_frac"] = stages["build_volume_gbs"] / peak
         stages["lookup_frac"] = stages["lookup_gbs"] / peak
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "kernel": kernel_name, "peak_source": peak_src,
+                "alg_bytes_per_launch": alg_bytes}
+    if vols is None and proj is None and args.precision in ("fp32", "tf32"):
+        # exact / TF32-rounded modes run the alt-corr kernel: FP32 CUDA-core work,
+        # (2r+2)^2 taps x 2C flops per pixel and level (windows not clipped at borders)
+        flops = M * hw * dc.levels * (2 * dc.radius + 2) ** 2 * 2 * wl.channels
+        fp32_peak = 148 * 128 * 2 * 1.965e9 / 1e12  # SMs x FP32 lanes x FMA x max clock
+        tfs = flops / (kern_ms * 1e-3) / 1e12
+        roofline = {"bound": "fp32", "achieved": tfs, "peak": fp32_peak, "unit": "TFLOP/s",
+                    "frac": tfs / fp32_peak, "kernel": "alt_lookup (FFMA gathered dots)",
+                    "peak_source": "nominal (148 SMs x 128 FP32 lanes x 2 flop x 1.965 GHz)",
+                    "alg_flops_per_launch": flops}
     traffic = None
     tpath = os.path.join(ROOT, "profiles", f"corr_tc_kernel_{wl.name}.md")
     if os.path.exists(tpath) and args.precision == "fp16" and vols is None:
         for ln in open(tpath):
             if ln.startswith("traffic_bytes_per_launch:"):
                 traffic = int(ln.split(":")[1])
-
+    roofline["traffic"] = traffic
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong" if wl.mode == "alt" else "weak",
@@ -525,10 +538,7 @@ def main():
                    "parallelism": f"edges sharded, dp{world}"},
         "gpu_launches": launches,
         "kernel_ms": kern_ms,
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": traffic,
-                     "kernel": kernel_name, "peak_source": peak_src,
-                     "alg_bytes_per_launch": alg_bytes},
+        "roofline": roofline,
         "e2e": {"value": M * world / (e2e_ms * 1e-3), "unit": UNIT,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
                 "pipelined": (f"{E2E_CHUNKS} edge chunks; input copy, compute and output copy "
