@@ -239,17 +239,43 @@ int dc_device_status(dc_ctx* ctx, dc_stream_t stream);
  * fused build + pyramid + lookup for M edges into out_dev, allocating nothing.
  *   - cfg is read as for dc_create (max_frames / max_edges are ignored);
  *     a packed store larger than 32 MiB is rejected with DC_ERR_INVALID_ARG
- *     (fp16 at 48x64x128: about 30 frames; at 54x96x128: 19 frames).
+ *     (fp16 at 48x64x128: 31 frames; at 54x96x128: 18 frames).
  *   - The array belongs to the current device and is kept until the process
  *     exits; the first call on each device looks up its address
  *     (cudaGetSymbolAddress), so make that first call before any stream
- *     capture.  Each call clears the parts that must start at zero.
+ *     capture.  Each call clears the parts that must start at zero (the
+ *     padding rows of the packed store).
+ *   - A bounded device-side wait that times out leaves `out` incomplete and is
+ *     reported by dc_static_device_status, not by this call's return value
+ *     (the call does not wait for the GPU).
  *   - All calls share the one array: calls that overlap on the GPU (other
  *     streams, other host threads) race and must be serialised by the caller.
  *   - Diagnostics go to stderr (there is no context for dc_last_error). */
 int dc_build_and_lookup_static(const dc_config* cfg, const void* fmaps_dev, int dtype,
                                int num_frames, const int* ii_dev, const int* jj_dev, int M,
                                const float* coords_dev, float* out_dev, dc_stream_t stream);
+
+/* Status of dc_build_and_lookup_static on the current device: waits for
+ * `stream`, then reports and clears the device error word of the static store
+ * (the counterpart of dc_device_status, which needs a context).  DC_OK, or
+ * DC_ERR_DEVICE_TIMEOUT when a bounded device-side wait of an earlier static
+ * call timed out -- that call's output is then incomplete.  The word keeps a
+ * time-out until this call reads it; all static calls on the device share it.
+ * Allocates nothing. */
+int dc_static_device_status(dc_stream_t stream);
+
+/* Test hook of the bounded device-side waits.  With wait_limit_ns > 0, every
+ * later launch of the fused tensor-core kernel in this process (all contexts
+ * and the static entry point) makes each CTA withhold its first source-tile
+ * load, so that the MMA warp's wait for it -- limited to wait_limit_ns instead
+ * of 2 s -- can end only by time-out.  The kernel then raises the device error
+ * word (DC_ERR_DEVICE_TIMEOUT from dc_device_status / dc_static_device_status),
+ * lets its copies in flight land, frees its tensor memory and returns; its
+ * output is incomplete and the context stays usable.  0 restores normal
+ * operation.  Change it only while no fused kernel is being launched from
+ * another host thread.  No reference counterpart (the reference has no
+ * device-side waits). */
+int dc_debug_inject_stall(long long wait_limit_ns);
 
 /* Number of kernel launches the library has issued on this context (for
  * launch accounting in benchmarks). */

@@ -38,6 +38,7 @@ def lib():
                                                 _fp, _fp, ctypes.c_int, _fp]
         L.ref_project.argtypes = [_fp, _fp, _fp, ctypes.c_int, _ip, _ip, ctypes.c_int,
                                   ctypes.c_int, ctypes.c_int, _fp, _fp]
+        L.ref_scatter_mean.argtypes = [_fp, ctypes.c_longlong, _ip, ctypes.c_int, _fp, _ip]
         _lib = L
     return _lib
 
@@ -109,3 +110,19 @@ def build_and_sample_fp16(fmaps, ii, jj, coords, alpha, want_vol0=False, iters=0
         float(alpha), _f(out), _f(vol0) if want_vol0 else None, int(iters), _f(ms))
     assert rc == 0
     return out, vol0, (float(ms[0]) if iters else None)
+
+
+def scatter_mean(feats, ii):
+    """The reference's GraphAgg loop on the GPU (memset, scale_add_kernel per edge
+    and per keyframe, main.cu:2262-2294; nn.cuh:381-385).  feats [E, ...];
+    returns (agg [K, ...], keyframe ids ascending)."""
+    feats = np.ascontiguousarray(feats, np.float32)
+    ii = np.ascontiguousarray(ii, np.int32)
+    E = feats.shape[0]
+    F = int(np.prod(feats.shape[1:]))
+    ids = np.unique(ii)
+    agg = np.empty((len(ids),) + feats.shape[1:], np.float32)
+    K = ctypes.c_int(0)
+    rc = lib().ref_scatter_mean(_f(feats), F, ii.ctypes.data_as(_ip), E, _f(agg), ctypes.byref(K))
+    assert rc == 0 and K.value == len(ids), rc
+    return agg, ids

@@ -16,9 +16,12 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <map>
+#include <set>
 #include <vector>
 
 #include "ref_kernels.cuh"
+#include "ref_nn.cuh"   // scale_add_kernel, nn.cuh:381-385
 #include "se3.cuh"  // the reference header, included where it lies (-I cuda_slam)
 
 #define RCHK(x)                                                                      \
@@ -58,7 +61,7 @@ struct DBuf {
 
 extern "C" {
 
-int ref_version(void) { return 2; }
+int ref_version(void) { return 3; }
 
 // projmap_kernel (se3.cuh:118-177) then batch_coords_hw2_to_2hw
 // (main.cu:1135-1146), as the update step launches them (main.cu:2188-2197).
@@ -252,6 +255,45 @@ int ref_build_and_sample_fp16(const float* fmaps_h, int K, int h, int w, const i
     }
     cublasDestroy(cublas);
     return rc;
+}
+
+// GraphAgg scatter-mean exactly as the update step runs it (main.cu:2262-2294):
+// a memset of the compact per-keyframe buffer, one scale_add_kernel launch
+// (dst += 1 * src) per edge in edge order, then one launch (dst += (1/n - 1) * dst)
+// per keyframe with n > 1 edges.  Compact order = ascending keyframe id
+// (std::set).  feats_h [E][F]; agg_h [K][F], K = number of distinct ii_h.
+int ref_scatter_mean(const float* feats_h, long long F, const int* ii_h, int E, float* agg_h,
+                     int* K_out) {
+    std::set<int> kf_set(ii_h, ii_h + E);
+    std::vector<int> kfs(kf_set.begin(), kf_set.end());
+    const int K = (int)kfs.size();
+    std::map<int, int> compact;
+    for (int i = 0; i < K; i++) compact[kfs[i]] = i;
+    DBuf<float> feats, agg;
+    RCHK(feats.alloc((size_t)E * F));
+    RCHK(agg.alloc((size_t)K * F));
+    RCHK(cudaMemcpy(feats.p, feats_h, (size_t)E * F * 4, cudaMemcpyHostToDevice));
+    RCHK(cudaMemset(agg.p, 0, (size_t)K * F * 4));
+    std::vector<int> count(K, 0);
+    const int n = (int)F;
+    for (int e = 0; e < E; e++) {
+        const int c = compact[ii_h[e]];
+        scale_add_kernel<<<(n + 255) / 256, 256>>>(agg.p + (size_t)c * F, feats.p + (size_t)e * F,
+                                                   1.0f, n);
+        count[c]++;
+    }
+    for (int i = 0; i < K; i++) {
+        if (count[i] > 1) {
+            float inv = 1.0f / (float)count[i];
+            scale_add_kernel<<<(n + 255) / 256, 256>>>(agg.p + (size_t)i * F, agg.p + (size_t)i * F,
+                                                       inv - 1.0f, n);
+        }
+    }
+    RCHK(cudaGetLastError());
+    RCHK(cudaDeviceSynchronize());
+    RCHK(cudaMemcpy(agg_h, agg.p, (size_t)K * F * 4, cudaMemcpyDeviceToHost));
+    if (K_out) *K_out = K;
+    return 0;
 }
 
 }  // extern "C"

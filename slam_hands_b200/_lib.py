@@ -70,6 +70,8 @@ SIGNATURES = {
     "dc_gather_rows": (_i, [_vp, _vp, _ll, _i, _vp, _i, _vp, _vp]),
     "dc_build_and_lookup_static": (_i, [ctypes.POINTER(DcConfig), _vp, _i, _i, _vp, _vp, _i,
                                         _vp, _vp, _vp]),
+    "dc_static_device_status": (_i, [_vp]),
+    "dc_debug_inject_stall": (_i, [_ll]),
 }
 
 _lib = None

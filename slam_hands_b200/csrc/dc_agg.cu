@@ -82,6 +82,9 @@ int dc_scatter_mean_impl(dc_ctx* ctx, const float* feats, long long F, const int
     std::sort(ids.begin(), ids.end());
     ids.erase(std::unique(ids.begin(), ids.end()), ids.end());
     const int K = (int)ids.size();
+    if (K > 65535)  // one grid row per keyframe
+        return dc_fail(ctx, DC_ERR_INVALID_ARG,
+                       "more than 65535 distinct source keyframes in one call");
     std::vector<int> offs(K + 1, 0), order(E);
     std::vector<int> compact(E);
     for (int e = 0; e < E; e++) {

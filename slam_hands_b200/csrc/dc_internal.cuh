@@ -122,6 +122,7 @@ int dc_check_launch(dc_ctx* ctx, const char* what);
 // Kernel entry points implemented in the .cu files.
 int dc_launch_store(dc_ctx* ctx, const void* fmaps, int dtype, int first, int count,
                     cudaStream_t s);
+int dc_launch_store_zero_padding(dc_ctx* ctx, int first, int count, cudaStream_t s);
 int dc_launch_volume_ffma(dc_ctx* ctx, const int* ii, const int* jj, int M, float* vol0,
                           cudaStream_t s);
 int dc_launch_volume_tc(dc_ctx* ctx, const int* ii, const int* jj, int M, float* vol0,

@@ -10,13 +10,15 @@
 // context lives here in one file-scope device array of fixed size, shared by
 // all calls in the process on a given GPU.
 #include <cstdio>
+#include <mutex>
 
 #include "dc_internal.cuh"
 
 namespace {
 
-// 32 MiB: room for 16 keyframes of a 54x96x128 fp16 pyramid (1.76 MB each),
-// or 30 of 48x64x128.  Every GPU that loads the library holds it until exit.
+// 32 MiB: room for 18 keyframes of a 54x96x128 fp16 pyramid (1.84 MB each),
+// or 31 of 48x64x128 (1.08 MB each).  Every GPU that loads the library holds it
+// until exit.
 constexpr size_t kScratchBytes = size_t(32) << 20;
 constexpr int kMaxDevices = 64;
 
@@ -31,17 +33,22 @@ struct DeviceScratch {
     int* err = nullptr;
 };
 DeviceScratch g_dev[kMaxDevices];
+std::mutex g_dev_mutex;  // first calls from several host threads fill g_dev safely
 
 int scratch_for_device(int dev, DeviceScratch** out) {
     if (dev < 0 || dev >= kMaxDevices) return DC_ERR_UNSUPPORTED;
+    std::lock_guard<std::mutex> lock(g_dev_mutex);
     DeviceScratch& d = g_dev[dev];
     if (!d.ready) {
-        if (cudaGetSymbolAddress(&d.store, g_scratch) != cudaSuccess ||
-            cudaGetSymbolAddress(reinterpret_cast<void**>(&d.err), g_scratch_err) !=
-                cudaSuccess) {
+        void* store = nullptr;
+        int* err = nullptr;
+        if (cudaGetSymbolAddress(&store, g_scratch) != cudaSuccess ||
+            cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_scratch_err) != cudaSuccess) {
             cudaGetLastError();
             return DC_ERR_CUDA;
         }
+        d.store = store;
+        d.err = err;
         d.ready = true;
     }
     *out = &d;
@@ -108,11 +115,12 @@ int dc_build_and_lookup_static(const dc_config* cfg, const void* fmaps, int dtyp
     ctx.dev_err = ds->err;
 
     cudaStream_t s = (cudaStream_t)stream;
-    // the store's padding rows and the error word must start at zero; the
-    // previous call left its contents behind
-    if (cudaMemsetAsync(ctx.store, 0, (size_t)ctx.store_bytes, s) != cudaSuccess ||
-        cudaMemsetAsync(ctx.dev_err, 0, sizeof(int), s) != cudaSuccess)
-        return fail(DC_ERR_CUDA, "clearing the static scratch failed");
+    // The previous call left its contents behind.  The packing kernel rewrites
+    // every data row; the padding rows (read as zero operand rows by the
+    // tensor-core kernel) are cleared here.  The error word is not cleared: it
+    // keeps a time-out until dc_static_device_status reads it.
+    rc = dc_launch_store_zero_padding(&ctx, 0, num_frames, s);
+    if (rc) return fail(rc, ctx.err.c_str());
     rc = dc_launch_store(&ctx, fmaps, dtype, 0, num_frames, s);
     if (rc) return fail(rc, ctx.err.c_str());
     if (dc_tc_supported(&ctx)) {
@@ -124,6 +132,27 @@ int dc_build_and_lookup_static(const dc_config* cfg, const void* fmaps, int dtyp
     }
     if (rc) return fail(rc, ctx.err.c_str());
     return DC_OK;
+}
+
+int dc_static_device_status(dc_stream_t stream) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return fail(DC_ERR_CUDA, "cudaGetDevice failed");
+    DeviceScratch* ds = nullptr;
+    if (scratch_for_device(dev, &ds) != DC_OK)
+        return fail(DC_ERR_CUDA, "cudaGetSymbolAddress of the static error word failed");
+    if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(DC_ERR_CUDA, "synchronising the stream failed");
+    }
+    int v = 0;
+    if (cudaMemcpy(&v, ds->err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+        return fail(DC_ERR_CUDA, "reading the static error word failed");
+    if (v == 0) return DC_OK;
+    if (cudaMemset(ds->err, 0, sizeof(int)) != cudaSuccess)
+        return fail(DC_ERR_CUDA, "clearing the static error word failed");
+    char msg[96];
+    std::snprintf(msg, sizeof msg, "a device-side wait timed out (site %d)", v);
+    return fail(DC_ERR_DEVICE_TIMEOUT, msg);
 }
 
 }  // extern "C"

@@ -108,7 +108,32 @@ int launch_store_t(dc_ctx* ctx, const void* fmaps, int first, int count, cudaStr
     return dc_check_launch(ctx, "store_pack_kernel");
 }
 
+// Zeroes the padding rows of store slots first .. first + count - 1: per level,
+// rows hw_l .. rows_l - 1 (rows_l = hw_l rounded up to DC_ROW_PAD), which the
+// tensor-core kernels read as operand rows and must hold zeros.  One CTA per
+// (slot, level); 16-byte stores.
+__global__ void __launch_bounds__(256) store_zero_padding_kernel(uint4* __restrict__ store,
+                                                                  dc::Geom g, int first,
+                                                                  int row_bytes) {
+    const int l = blockIdx.y, slot = first + blockIdx.x;
+    const long long hw_l = (long long)g.H[l] * g.W[l];
+    const long long rows_l = (hw_l + DC_ROW_PAD - 1) / DC_ROW_PAD * DC_ROW_PAD;
+    const long long r0 = (long long)slot * g.frame_rows + g.row0[l] + hw_l;
+    const long long n16 = (rows_l - hw_l) * row_bytes / 16;
+    uint4* p = store + r0 * row_bytes / 16;
+    for (long long i = threadIdx.x; i < n16; i += blockDim.x) p[i] = make_uint4(0, 0, 0, 0);
+}
+
 }  // namespace
+
+int dc_launch_store_zero_padding(dc_ctx* ctx, int first, int count, cudaStream_t s) {
+    if (count <= 0) return DC_OK;
+    dim3 grid(count, ctx->cfg.levels);
+    store_zero_padding_kernel<<<grid, 256, 0, s>>>(static_cast<uint4*>(ctx->store),
+                                                  dc::geom_of(ctx), first,
+                                                  ctx->cfg.channels * ctx->elem_bytes);
+    return dc_check_launch(ctx, "store_zero_padding_kernel");
+}
 
 int dc_launch_store(dc_ctx* ctx, const void* fmaps, int dtype, int first, int count,
                     cudaStream_t s) {

@@ -39,6 +39,7 @@
 // copies in flight, frees its TMEM and returns.  No TMA multicast is used.
 #include <cuda.h>
 
+#include <atomic>
 #include <cstring>
 
 #include "dc_internal.cuh"
@@ -136,6 +137,8 @@ struct TcParams {
     int atoms;        // 128-byte K atoms per operand row (C * 2 / 128)
     uint32_t ab_fmt;  // 0 fp16, 1 bf16
     int M;            // edges
+    int stall;        // test hook: withhold each CTA's first source-tile load
+    unsigned long long wait_ns;  // limit of the pipeline waits (the drain waits keep 2 s)
 };
 
 struct TileInfo {
@@ -209,11 +212,11 @@ __device__ long long g_tc_trace[8 * 1024];
 // All lanes of a warp wait for one barrier phase: lane 0 polls (bounded), the
 // others then observe the completed phase.  Returns false on a time-out.
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort,
-                                          int lane) {
+                                          int lane, unsigned long long limit_ns) {
     int ok = 1;
-    if (lane == 0) ok = mbar_wait(bar, parity, abort) ? 1 : 0;
+    if (lane == 0) ok = mbar_wait(bar, parity, abort, limit_ns) ? 1 : 0;
     ok = __shfl_sync(0xffffffffu, ok, 0);
-    if (ok) mbar_wait(bar, parity, abort);
+    if (ok) mbar_wait(bar, parity, abort, limit_ns);
     return ok != 0;
 }
 
@@ -384,7 +387,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         DC_TC_LOAD_COORDS(blockIdx.x);  // all loads of a tile in flight at once
         for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x, i++) {
             const int tb = i & 1;
-            if (i >= 2 && !warp_wait(bar(kBarSEmpty + tb), ((i >> 1) - 1) & 1, abort, lane)) {
+            if (i >= 2 && !warp_wait(bar(kBarSEmpty + tb), ((i >> 1) - 1) & 1, abort, lane, P.wait_ns)) {
                 if (lane == 0) raise_abort(abort, P.err, 1);
                 break;
             }
@@ -476,25 +479,27 @@ __global__ void __launch_bounds__(kThreads, 1)
                 int lv = 0;
                 for (int c = 0; c <= ti.n; c++) {
                     if (c == pre) {
-                        if (na >= 1 && !mbar_wait(bar(kBarAEmpty), (na - 1) & 1, abort)) {
+                        if (na >= 1 && !mbar_wait(bar(kBarAEmpty), (na - 1) & 1, abort, P.wait_ns)) {
                             raise_abort(abort, P.err, 3);
                             break;
                         }
-                        mbar_arrive_expect_tx(bar(kBarAFull), P.atoms * kTileM * kRowBytes);
-                        const int arow =
-                            (int)((long long)ti.si * g.frame_rows + g.row0[0] + ti.p0);
-                        for (int k = 0; k < P.atoms; k++)
-                            tma_load_2d(sA + k * kTileM * kRowBytes, &maps.a, k * 64, arow,
-                                        bar(kBarAFull));
-                        a_issued = 1;
-                        a_parity = na & 1;
+                        if (!(P.stall && na == 0)) {
+                            mbar_arrive_expect_tx(bar(kBarAFull), P.atoms * kTileM * kRowBytes);
+                            const int arow =
+                                (int)((long long)ti.si * g.frame_rows + g.row0[0] + ti.p0);
+                            for (int k = 0; k < P.atoms; k++)
+                                tma_load_2d(sA + k * kTileM * kRowBytes, &maps.a, k * 64, arow,
+                                            bar(kBarAFull));
+                            a_issued = 1;
+                            a_parity = na & 1;
+                        }
                     }
                     if (c == ti.n) break;
                     while (c >= sch[lv].first + sch[lv].count) lv++;
                     const int s = gc % kStagesB;
                     const long long t0 = DC_PROF_NOW();
                     if (gc >= kStagesB &&
-                        !mbar_wait(bar(kBarEmpty + s), ((gc / kStagesB) - 1) & 1, abort)) {
+                        !mbar_wait(bar(kBarEmpty + s), ((gc / kStagesB) - 1) & 1, abort, P.wait_ns)) {
                         raise_abort(abort, P.err, 4);
                         break;
                     }
@@ -526,9 +531,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // ---- MMA issuer
         int gc = 0, na = 0, i = 0;
+        int last_mma = -1;  // global chunk index of the last committed MMA group
         for (int t = blockIdx.x; t < ntiles; t += gridDim.x, i++) {
             const int tb = i & 1;
-            if (!warp_wait(bar(kBarSFull + tb), (i >> 1) & 1, abort, lane)) {
+            if (!warp_wait(bar(kBarSFull + tb), (i >> 1) & 1, abort, lane, P.wait_ns)) {
                 if (lane == 0) raise_abort(abort, P.err, 5);
                 break;
             }
@@ -536,7 +542,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const LevelSched* sch = sched_base + tb * DC_MAX_LEVELS;
             bool ok = true;
             if (lane == 0 && ti.n > 0) {
-                if (!mbar_wait(bar(kBarAFull), na & 1, abort)) {
+                if (!mbar_wait(bar(kBarAFull), na & 1, abort, P.wait_ns)) {
                     raise_abort(abort, P.err, 6);
                     ok = false;
                 } else {
@@ -547,7 +553,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         while (c >= sch[lv].first + sch[lv].count) lv++;
                         const int s = gc % kStagesB, a = gc % kAcc;
                         const long long t0 = DC_PROF_NOW();
-                        if (!mbar_wait(bar(kBarFull + s), (gc / kStagesB) & 1, abort)) {
+                        if (!mbar_wait(bar(kBarFull + s), (gc / kStagesB) & 1, abort, P.wait_ns)) {
                             raise_abort(abort, P.err, 7);
                             ok = false;
                             break;
@@ -556,7 +562,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         w_a += t1 - t0;
                         DC_TRACE(1, gc);
                         if (gc >= kAcc &&
-                            !mbar_wait(bar(kBarTEmpty + a), ((gc / kAcc) - 1) & 1, abort)) {
+                            !mbar_wait(bar(kBarTEmpty + a), ((gc / kAcc) - 1) & 1, abort, P.wait_ns)) {
                             raise_abort(abort, P.err, 8);
                             ok = false;
                             break;
@@ -576,6 +582,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                         mma_commit(bar(kBarEmpty + s));
                         mma_commit(bar(kBarTFull + a));
+                        last_mma = gc;
                         DC_TRACE(3, gc);
                     }
                     mma_commit(bar(kBarAEmpty));  // the source tile may be replaced
@@ -585,6 +592,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             if (lane == 0) mbar_arrive(bar(kBarSEmpty + tb));
             if (!ok) break;
+        }
+        if (lane == 0 && *abort && last_mma >= 0) {
+            // the MMAs issued so far read shared memory and write TMEM: let them
+            // finish (bounded) before the CTA frees TMEM and exits
+            mbar_wait(bar(kBarEmpty + last_mma % kStagesB), (last_mma / kStagesB) & 1, nullptr);
         }
         if (lane == 0) {
             DC_PROF_STORE(2, w_a);
@@ -623,7 +635,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float cx = cx_next, cy = cy_next;
             DC_TC_PIXEL_COORDS(t + gridDim.x);
             const long long t0s = DC_PROF_NOW();
-            if (!warp_wait(bar(kBarSFull + tb), (i >> 1) & 1, abort, lane)) {
+            if (!warp_wait(bar(kBarSFull + tb), (i >> 1) & 1, abort, lane, P.wait_ns)) {
                 if (lane == 0) raise_abort(abort, P.err, 9);
                 break;
             }
@@ -655,7 +667,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int c = 0; c < Ls.count; c++, gc++) {
                     const int a = gc % kAcc;
                     const long long t0 = DC_PROF_NOW();
-                    if (!warp_wait(bar(kBarTFull + a), (gc / kAcc) & 1, abort, lane)) {
+                    if (!warp_wait(bar(kBarTFull + a), (gc / kAcc) & 1, abort, lane, P.wait_ns)) {
                         if (lane == 0) raise_abort(abort, P.err, 10);
                         alive = false;
                         break;
@@ -778,7 +790,17 @@ LevelBox level_box(const dc_ctx* ctx, int l) {
     return b;
 }
 
+// Process-wide test hook of the bounded waits (dc_debug_inject_stall)
+// (> 0: stall active, with this wait limit in ns)
+std::atomic<long long> g_test_wait_ns{0};
+
 }  // namespace
+
+extern "C" int dc_debug_inject_stall(long long wait_limit_ns) {
+    if (wait_limit_ns < 0) return DC_ERR_INVALID_ARG;
+    g_test_wait_ns.store(wait_limit_ns);
+    return DC_OK;
+}
 
 #ifdef DC_TC_PROFILE
 extern "C" int dc_tc_profile_read(unsigned long long* host, int n) {
@@ -853,6 +875,11 @@ int dc_launch_tc(dc_ctx* ctx, const int* ii, const int* jj, int M, const float* 
     P.atoms = ctx->cfg.channels * 2 / 128;
     P.ab_fmt = ctx->cfg.precision == DC_PREC_BF16 ? 1u : 0u;
     P.M = M;
+    // the short limit only ever comes with the stall: then no barrier phase the
+    // epilogue warps wait on completes, so they all give up at the same chunk
+    const long long lim = g_test_wait_ns.load();
+    P.stall = lim > 0;
+    P.wait_ns = lim > 0 ? (unsigned long long)lim : 2000000000ull;
     const Layout Ly = make_layout(P.atoms);
     const size_t smem = Ly.total + 1024;
     const int ntiles = (ctx->hw + kTileM - 1) / kTileM * M;

@@ -55,3 +55,21 @@ def test_gather_rows_exact(cuda, shape):
     for e, r in enumerate(idx):
         exp = src[r] if 0 <= r < 12 else np.zeros(shape, np.float32)
         assert np.array_equal(got[e], exp)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("E,shape", [(48, (128, 48, 64)), (13, (3, 7, 9))])
+def test_scatter_mean_bit_exact_vs_reference_kernel(cuda, E, shape):
+    # the reference's own loop on the GPU: memset, scale_add_kernel per edge and
+    # per keyframe (main.cu:2262-2294, nn.cuh:381-385), built into oracle/_ref
+    from oracle import ref as REF
+    if not REF.available():
+        pytest.skip("oracle/_ref not built")
+    rng = np.random.default_rng(100 + E)
+    feats = rng.standard_normal((E,) + shape, dtype=np.float32)
+    ii = rng.integers(0, max(2, E // 3), E).astype(np.int32)
+    dc = DroidCorrelation(12, 16, max_frames=4, max_edges=64)
+    agg, ids = dc.scatter_mean(torch.from_numpy(feats).cuda(), ii)
+    ref, ref_ids = REF.scatter_mean(feats, ii)
+    assert np.array_equal(ids, ref_ids)
+    assert np.array_equal(agg.cpu().numpy(), ref)
