@@ -288,8 +288,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     corr_tc_kernel(const __grid_constant__ TcMaps maps, TcParams P) {
     constexpr int D = 2 * R + 1, NW = 2 * R + 2;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* base = reinterpret_cast<uint8_t*>(
-        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // 1024-byte aligned base by pointer arithmetic on the shared array itself, so
+    // that the compiler keeps the shared address space (LDS/STS, not generic)
+    uint8_t* base = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     constexpr Layout Ly2 = make_layout(2);
     const Layout Ly = P.atoms == 2 ? Ly2 : make_layout(P.atoms);
     const dc::Geom& g = P.g;

@@ -41,8 +41,9 @@ struct VolParams {
 __global__ void __launch_bounds__(kThreadsV, 2)
     volume_tc_kernel(const __grid_constant__ CUtensorMap tmap, VolParams P) {
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* base = reinterpret_cast<uint8_t*>(
-        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // 1024-byte aligned base by pointer arithmetic on the shared array itself, so
+    // that the compiler keeps the shared address space (LDS/STS, not generic)
+    uint8_t* base = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int e = blockIdx.y;
     const int tp = blockIdx.x / P.tiles_q, tq = blockIdx.x % P.tiles_q;
