@@ -26,6 +26,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -77,7 +78,7 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.idx = gpu_index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{gpu_index}.csv")
+        self.path = os.path.join(tempfile.gettempdir(), f"dc_bench_clocks_gpu{gpu_index}_{os.getpid()}.csv")
 
     def start(self):
         try:
