@@ -277,6 +277,14 @@ int dc_static_device_status(dc_stream_t stream);
  * device-side waits). */
 int dc_debug_inject_stall(long long wait_limit_ns);
 
+/* Cap the CTAs of the persistent fused tensor-core kernel (dc_build_and_lookup,
+ * fp16 / bf16) at max_ctas; 0 (the default) runs one CTA per SM.  Each CTA
+ * holds a whole SM, so a kernel on another stream -- e.g. the NCCL broadcast
+ * of the next step's keyframe -- can only run beside it on SMs left free.
+ * Results do not depend on the cap.  No reference counterpart (one GPU, one
+ * stream in the reference). */
+int dc_set_max_ctas(dc_ctx* ctx, int max_ctas);
+
 /* Number of kernel launches the library has issued on this context (for
  * launch accounting in benchmarks). */
 long long dc_launch_count(const dc_ctx* ctx);

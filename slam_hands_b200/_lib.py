@@ -71,6 +71,7 @@ SIGNATURES = {
     "dc_build_and_lookup_static": (_i, [ctypes.POINTER(DcConfig), _vp, _i, _i, _vp, _vp, _i,
                                         _vp, _vp, _vp]),
     "dc_static_device_status": (_i, [_vp]),
+    "dc_set_max_ctas": (_i, [_vp, _i]),
     "dc_debug_inject_stall": (_i, [_ll]),
 }
 

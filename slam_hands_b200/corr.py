@@ -105,6 +105,11 @@ class DroidCorrelation:
         return int(self.lib.dc_launch_count(self._ctx))
 
     # -- feature-map store -----------------------------------------------------
+    def set_max_ctas(self, max_ctas: int) -> None:
+        """Cap the persistent fused kernel's CTAs (0 = one per SM), leaving SMs
+        free for work on other streams (dc_set_max_ctas)."""
+        self._check(self.lib.dc_set_max_ctas(self._ctx, int(max_ctas)))
+
     def set_frames(self, fmaps: torch.Tensor, first_slot: int = 0,
                    stream: Optional[torch.cuda.Stream] = None) -> None:
         """Pack fmaps [K, C, h, w] (fp32 or fp16) into slots first_slot..+K."""

@@ -146,6 +146,13 @@ long long dc_context_bytes(const dc_ctx* ctx) { return ctx ? ctx->store_bytes : 
 
 long long dc_launch_count(const dc_ctx* ctx) { return ctx ? ctx->launches : 0; }
 
+int dc_set_max_ctas(dc_ctx* ctx, int max_ctas) {
+    if (!ctx) return DC_ERR_INVALID_ARG;
+    if (max_ctas < 0) return dc_fail(ctx, DC_ERR_INVALID_ARG, "max_ctas < 0");
+    ctx->max_ctas = max_ctas;
+    return DC_OK;
+}
+
 int dc_set_frames(dc_ctx* ctx, const void* fmaps, int dtype, int first, int count,
                   dc_stream_t stream) {
     if (!ctx) return DC_ERR_INVALID_ARG;

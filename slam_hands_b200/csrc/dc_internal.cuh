@@ -33,6 +33,7 @@ struct dc_ctx {
     void* store = nullptr;  // device
     long long store_bytes = 0;
     int num_sms = 148;
+    int max_ctas = 0;  // cap on the CTAs of the persistent fused kernel (0: one per SM)
     long long launches = 0;
     int* dev_err = nullptr;  // device error word raised by bounded device waits; the same
                              // allocation holds the scatter-mean lists from word 32 on

@@ -884,7 +884,8 @@ int dc_launch_tc(dc_ctx* ctx, const int* ii, const int* jj, int M, const float* 
     const Layout Ly = make_layout(P.atoms);
     const size_t smem = Ly.total + 1024;
     const int ntiles = (ctx->hw + kTileM - 1) / kTileM * M;
-    dim3 grid(ntiles < ctx->num_sms ? ntiles : ctx->num_sms);
+    const int ctas = ctx->max_ctas > 0 && ctx->max_ctas < ctx->num_sms ? ctx->max_ctas : ctx->num_sms;
+    dim3 grid(ntiles < ctas ? ntiles : ctas);
     TcMaps maps;
     memset(&maps, 0, sizeof(maps));
     memcpy(&maps.a, ctx->tmap_a, sizeof(CUtensorMap));

@@ -61,10 +61,48 @@ def peers_alive(store, step: int, world: int, rank: int, timeout_s: float = 1.0)
     return missing
 
 
-def replicate_store(dc, first_slot: int, count: int, src: int = 0, group=None) -> None:
+def replicate_store(dc, first_slot: int, count: int, src: int = 0, group=None,
+                    timeout_s: float = None) -> None:
     """Broadcast packed store slots from rank `src` (after its set_frames), so the
     other ranks skip packing: the packed fp16 pyramid is smaller than the fp32
-    maps and identical on every rank."""
+    maps and identical on every rank.  The collective runs on the current CUDA
+    stream.  With `timeout_s`, a peer that never joins makes this raise
+    RuntimeError after that many seconds instead of blocking (pair it with
+    `peers_alive` between steps, so that a dead peer is noticed before the
+    collective is entered)."""
+    import datetime
+
     import torch.distributed as dist
 
-    dist.broadcast(dc.store_slots(first_slot, count), src=src, group=group)
+    buf = dc.store_slots(first_slot, count)
+    if timeout_s is None:
+        dist.broadcast(buf, src=src, group=group)
+        return
+    work = dist.broadcast(buf, src=src, group=group, async_op=True)
+    work.wait(timeout=datetime.timedelta(seconds=timeout_s))
+
+
+class SlotRing:
+    """Keyframe slots of the packed store with one spare slot, so that a new
+    keyframe can be packed (and broadcast) while kernels of the previous step
+    still read the old ones.
+
+    The store holds `frames + 1` slots.  Logical keyframe f lives in physical
+    slot `phys[f]`; `spare` is unused.  `begin(f)` names the slot that receives
+    f's new feature map (the spare); `commit(f)` makes it f's slot and the old
+    one the spare.  Edge lists are given in logical ids and translated with
+    `slots(ii)`.  (The reference stores keyframe k in DroidState::fmaps[k],
+    cuda_slam/main.cu:755, synchronously, on one GPU.)"""
+
+    def __init__(self, frames: int):
+        self.phys = list(range(frames))
+        self.spare = frames
+
+    def begin(self, f: int) -> int:
+        return self.spare
+
+    def commit(self, f: int) -> None:
+        self.phys[f], self.spare = self.spare, self.phys[f]
+
+    def slots(self, ids):
+        return [self.phys[int(i)] for i in ids]

@@ -69,7 +69,14 @@ def _failing_worker(rank, world, port, q):
     # and a broadcast entered anyway ends with an error after its deadline
     from datetime import timedelta
 
-    from slam_hands_b200.shard import peers_alive, replicate_frames
+    from slam_hands_b200.shard import peers_alive, replicate_frames, replicate_store
+
+    class _Store:  # a context's packed slots, as a host tensor (gloo runs on CPU)
+        def __init__(self):
+            self.buf = torch.zeros(64, dtype=torch.uint8)
+
+        def store_slots(self, first, count):
+            return self.buf
 
     store = dist.TCPStore("127.0.0.1", port, world, rank == 0, timeout=timedelta(seconds=30))
     dist.init_process_group("gloo", store=store, rank=rank, world_size=world,
@@ -83,11 +90,14 @@ def _failing_worker(rank, world, port, q):
         return  # "fails": no heartbeat for step 1, never joins again
     missing1 = peers_alive(store, 1, world, rank, timeout_s=1.0)
     store.wait(["dc_test/rank1_done"])
-    try:
-        replicate_frames(fm, timeout_s=1.0)
-        raised = False
-    except RuntimeError:
-        raised = True
+    raised = []
+    for fn in (lambda: replicate_frames(fm, timeout_s=1.0),
+               lambda: replicate_store(_Store(), 0, 1, timeout_s=1.0)):
+        try:
+            fn()
+            raised.append(False)
+        except RuntimeError:
+            raised.append(True)
     q.put((rank, missing0, missing1, raised))
     q.close()
     q.join_thread()  # flush the result before the hard exit
@@ -107,4 +117,17 @@ def test_dead_rank_detected_on_host_gloo():
         p.join(timeout=60)
     assert res[1][1] == [] and res[0][1] == []      # step 0: all heartbeats present
     assert res[0][2] == [1]                          # step 1: rank 1 reported missing
-    assert res[0][3] is True                         # a broadcast entered anyway errors out
+    assert res[0][3] == [True, True]                 # broadcasts entered anyway error out
+
+
+def test_slot_ring_keeps_a_spare_slot():
+    from slam_hands_b200.shard import SlotRing
+    ring = SlotRing(4)
+    assert ring.slots([0, 1, 2, 3]) == [0, 1, 2, 3] and ring.spare == 4
+    for k in range(9):
+        f = k % 4
+        new = ring.begin(f)
+        old = ring.phys[f]
+        ring.commit(f)
+        assert ring.phys[f] == new and ring.spare == old
+        assert sorted(ring.phys + [ring.spare]) == list(range(5))  # a permutation of the slots
