@@ -296,6 +296,10 @@ def main():
     if pg is not None:
         if peers_alive(store, -1, world, rank, timeout_s=60.0):
             raise RuntimeError("a rank did not join")
+        # NCCL sets up its communicator on the first collective: not part of the copy
+        warm = torch.zeros(1, device=dev)
+        pg.all_reduce(warm)
+        torch.cuda.synchronize()
         ra, rb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         ra.record(stream)
         replicate_store(dc, 0, wl.frames, timeout_s=BCAST_TIMEOUT_S)

@@ -225,6 +225,31 @@ int dc_scatter_mean(dc_ctx* ctx, const float* feats_dev, long long F, const int*
 int dc_gather_rows(dc_ctx* ctx, const float* src_dev, long long F, int num_rows,
                    const int* idx_dev, int n, float* dst_dev, dc_stream_t stream);
 
+/* The update operator's correlation encoder, first layer (UpdateModule
+ * corr_enc_0: a 1x1 convolution levels*(2r+1)^2 = 196 -> 128 with bias,
+ * main.cu:552-553, then relu_inplace and round_to_fp16, main.cu:603-606), on
+ * the tensor cores.  dc_set_corr_encoder packs the layer's weights once:
+ *   weight_dev [128][196] fp32 (the convolution's [co][ci][1][1] weights)
+ *   bias_dev   [128] fp32;  out_channels must be 128.
+ * The context allocates 64 KB for the packed weights on the first call. */
+int dc_set_corr_encoder(dc_ctx* ctx, const float* weight_dev, const float* bias_dev,
+                        int out_channels, dc_stream_t stream);
+
+/* out = fp16(relu(W corr + b)) per pixel: corr_dev [M][196][h][w] fp32 (the
+ * lookup's output), out_dev [M][128][h][w] fp16 -- the values the reference
+ * holds as fp16-rounded floats, stored in half the bytes.  Features and
+ * weights are rounded to fp16 for the tensor cores, fp32 accumulation. */
+int dc_corr_encode(dc_ctx* ctx, const float* corr_dev, int M, void* out_dev, dc_stream_t stream);
+
+/* dc_build_and_lookup into corr_dev (caller-owned [M][196][h][w], the
+ * reference's batch_corr buffer, main.cu:1336), then dc_corr_encode into
+ * out_dev: the update step's correlation features and their encoding
+ * (main.cu:2200 then :603-606) back to back, so that the 196-channel features
+ * are read by the encoder while they are still in L2. */
+int dc_build_lookup_encode(dc_ctx* ctx, const int* ii_dev, const int* jj_dev, int M,
+                           const float* coords_dev, float* corr_dev, void* out_dev,
+                           dc_stream_t stream);
+
 /* Wait for `stream`, then report and clear the device error word that the
  * library's bounded device-side waits raise when they time out: DC_OK or
  * DC_ERR_DEVICE_TIMEOUT.  (The reference has no device-side waits.) */

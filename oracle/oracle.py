@@ -242,3 +242,16 @@ def scatter_mean(feats: np.ndarray, ii) -> tuple:
     ids = np.empty(E, np.int32)
     K = lib().orc_scatter_mean(_f(feats), F, _i(ii), E, _f(agg), _i(ids))
     return agg[:K].reshape((K,) + feats.shape[1:]), ids[:K].copy()
+
+
+def corr_encode(corr: np.ndarray, weight: np.ndarray, bias: np.ndarray) -> np.ndarray:
+    """The update operator's first correlation-encoder layer as the reference
+    computes it: a 1x1 convolution 196 -> 128 with bias (UpdateModule corr_enc_0,
+    cuda_slam/main.cu:552-553), relu_inplace, round_to_fp16 (main.cu:603-606).
+    Here in float64 before the final ReLU and fp16 rounding.
+    corr [M, ci, h, w], weight [co, ci] (or [co, ci, 1, 1]), bias [co]
+    -> [M, co, h, w] float16."""
+    w = np.asarray(weight, np.float64).reshape(weight.shape[0], -1)
+    x = np.asarray(corr, np.float64)
+    y = np.einsum("oc,mchw->mohw", w, x) + np.asarray(bias, np.float64)[None, :, None, None]
+    return np.maximum(y, 0.0).astype(np.float16)

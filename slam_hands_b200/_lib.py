@@ -72,6 +72,9 @@ SIGNATURES = {
                                         _vp, _vp, _vp]),
     "dc_static_device_status": (_i, [_vp]),
     "dc_set_max_ctas": (_i, [_vp, _i]),
+    "dc_set_corr_encoder": (_i, [_vp, _vp, _vp, _i, _vp]),
+    "dc_corr_encode": (_i, [_vp, _vp, _i, _vp, _vp]),
+    "dc_build_lookup_encode": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp, _vp]),
     "dc_debug_inject_stall": (_i, [_ll]),
 }
 

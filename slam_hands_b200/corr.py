@@ -215,6 +215,58 @@ class DroidCorrelation:
         """Fused build + pyramid + lookup (no volume in memory)."""
         return self._edge_call(self.lib.dc_build_and_lookup, ii, jj, coords, out, stream)
 
+    # -- correlation encoder (corr_enc_0 + ReLU + fp16, main.cu:552-553, :603-606) --
+    def set_corr_encoder(self, weight: torch.Tensor, bias: torch.Tensor,
+                         stream: Optional[torch.cuda.Stream] = None) -> None:
+        """weight [128, 196] (or [128, 196, 1, 1]) fp32, bias [128] fp32."""
+        w = weight.reshape(weight.shape[0], -1).contiguous()
+        if w.shape != (128, self.out_channels):
+            raise ValueError(f"weight must be [128, {self.out_channels}]")
+        self._cuda(w, torch.float32, "weight")
+        self._cuda(bias, torch.float32, "bias")
+        self._enc_keep = (w, bias)  # the packing kernel reads them on `stream`
+        self._check(self.lib.dc_set_corr_encoder(self._ctx, w.data_ptr(), bias.data_ptr(),
+                                                 w.shape[0], _stream(stream)))
+
+    def corr_encode(self, corr: torch.Tensor, out: Optional[torch.Tensor] = None,
+                    stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+        """fp16(relu(W corr + b)): corr [M, 196, h, w] fp32 -> [M, 128, h, w] fp16."""
+        self._cuda(corr, torch.float32, "corr")
+        M = corr.shape[0]
+        if corr.shape != (M, self.out_channels, self.h, self.w):
+            raise ValueError(f"corr must be [M, {self.out_channels}, {self.h}, {self.w}]")
+        if out is None:
+            out = torch.empty(M, 128, self.h, self.w, dtype=torch.float16, device=self.device)
+        self._cuda(out, torch.float16, "out")
+        self._check(self.lib.dc_corr_encode(self._ctx, corr.data_ptr(), M, out.data_ptr(),
+                                            _stream(stream)))
+        return out
+
+    def build_lookup_encode(self, ii, jj, coords: torch.Tensor,
+                            corr: Optional[torch.Tensor] = None,
+                            out: Optional[torch.Tensor] = None,
+                            stream: Optional[torch.cuda.Stream] = None):
+        """Fused correlation into `corr` [M, 196, h, w], then its encoding.
+        Returns (out [M, 128, h, w] fp16, corr)."""
+        ii, jj = self._edges(ii, jj)
+        M = ii.numel()
+        self._cuda(coords, torch.float32, "coords")
+        if coords.shape != (M, 2, self.h, self.w):
+            raise ValueError(f"coords must be [{M}, 2, {self.h}, {self.w}]")
+        if corr is None:
+            corr = torch.empty(M, self.out_channels, self.h, self.w, device=self.device)
+        if out is None:
+            out = torch.empty(M, 128, self.h, self.w, dtype=torch.float16, device=self.device)
+        self._cuda(corr, torch.float32, "corr")
+        self._cuda(out, torch.float16, "out")
+        s = _stream(stream)
+        for c0 in range(0, M, self.max_edges):
+            m = min(self.max_edges, M - c0)
+            self._check(self.lib.dc_build_lookup_encode(
+                self._ctx, ii[c0].data_ptr(), jj[c0].data_ptr(), m, coords[c0].data_ptr(),
+                corr[c0].data_ptr(), out[c0].data_ptr(), s))
+        return out, corr
+
     def _project_args(self, poses, disps, intrinsics):
         self._cuda(poses, torch.float32, "poses")
         self._cuda(disps, torch.float32, "disps")

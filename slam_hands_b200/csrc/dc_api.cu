@@ -135,6 +135,7 @@ int dc_destroy(dc_ctx* ctx) {
     cudaSetDevice(ctx->device);
     if (ctx->store) cudaFree(ctx->store);
     if (ctx->dev_err) cudaFree(ctx->dev_err);
+    if (ctx->enc_w) cudaFree(ctx->enc_w);
     if (prev >= 0) cudaSetDevice(prev);
     delete ctx;
     return DC_OK;
@@ -285,6 +286,32 @@ int dc_gather_rows(dc_ctx* ctx, const float* src, long long F, int num_rows, con
     if (n == 0) return DC_OK;
     if (!src || !idx || !dst) return dc_fail(ctx, DC_ERR_INVALID_ARG, "NULL pointer");
     return dc_gather_rows_impl(ctx, src, F, num_rows, idx, n, dst, (cudaStream_t)stream);
+}
+
+int dc_set_corr_encoder(dc_ctx* ctx, const float* weight, const float* bias, int out_channels,
+                        dc_stream_t stream) {
+    if (!ctx) return DC_ERR_INVALID_ARG;
+    if (!weight || !bias) return dc_fail(ctx, DC_ERR_INVALID_ARG, "NULL pointer");
+    return dc_set_corr_encoder_impl(ctx, weight, bias, out_channels, (cudaStream_t)stream);
+}
+
+int dc_corr_encode(dc_ctx* ctx, const float* corr, int M, void* out, dc_stream_t stream) {
+    if (!ctx) return DC_ERR_INVALID_ARG;
+    if (M < 0) return dc_fail(ctx, DC_ERR_INVALID_ARG, "M < 0");
+    if (M == 0) return DC_OK;
+    if (!corr || !out) return dc_fail(ctx, DC_ERR_INVALID_ARG, "NULL pointer");
+    return dc_launch_encoder(ctx, corr, M, out, (cudaStream_t)stream);
+}
+
+int dc_build_lookup_encode(dc_ctx* ctx, const int* ii, const int* jj, int M, const float* coords,
+                           float* corr, void* out, dc_stream_t stream) {
+    if (!ctx) return DC_ERR_INVALID_ARG;
+    if (!ctx->enc_ready)
+        return dc_fail(ctx, DC_ERR_NOT_READY, "dc_set_corr_encoder has not been called");
+    if (M > 0 && (!corr || !out)) return dc_fail(ctx, DC_ERR_INVALID_ARG, "NULL pointer");
+    int rc = dc_build_and_lookup(ctx, ii, jj, M, coords, corr, stream);
+    if (rc) return rc;
+    return dc_corr_encode(ctx, corr, M, out, stream);
 }
 
 int dc_device_status(dc_ctx* ctx, dc_stream_t stream) {

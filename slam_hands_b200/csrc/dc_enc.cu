@@ -1,0 +1,226 @@
+// dc_enc.cu -- the update operator's correlation encoder, first layer, on the
+// tensor cores: out = fp16(relu(W corr + b)), a 1x1 convolution from the
+// lookup's levels*(2r+1)^2 = 196 channels to 128.
+//
+// Replaces UpdateModule's corr_enc_0 (cuDNN 1x1 convolution, 196 -> 128, with
+// bias; cuda_slam/main.cu:552-553) followed by relu_inplace and round_to_fp16
+// (main.cu:603-606), which read the 196-channel fp32 correlation features and
+// write 128 fp32 channels holding fp16-rounded values.  Here the result is
+// written as fp16 (the same values, half the bytes).
+//
+// Per tile of 128 pixels of one edge (persistent CTAs, 128 threads): thread p
+// reads pixel p's 196 features (coalesced along pixels), rounds them to fp16
+// and writes them to shared memory as the K-major A operand (128-byte swizzle,
+// K padded with zeros to 256); the weights, packed once by dc_set_corr_encoder
+// into the same layout, stay resident in shared memory as the B operand; one
+// thread issues 16 tcgen05.mma (kind::f16, M = N = 128, K = 16) into a TMEM
+// accumulator; each warp reads its 32 pixels' 128 outputs back (tcgen05.ld),
+// adds the bias, applies the ReLU, rounds to fp16 and stores 64-byte rows.
+// The wait for the MMAs is bounded (2 s) and reports through the context's
+// device error word.
+#include <cuda_fp16.h>
+
+#include "dc_internal.cuh"
+#include "dc_sm100.cuh"
+
+namespace {
+
+using namespace dc::sm100;
+
+constexpr int kEncM = 128;        // pixels per tile (MMA M, TMEM lanes)
+constexpr int kEncCo = 128;       // output channels (MMA N)
+constexpr int kEncK = 256;        // input channels, padded (four 64-element K atoms)
+constexpr int kEncThreads = 128;
+constexpr uint32_t kAtomBytes = 128u * 128u;            // 128 rows x 128 bytes
+constexpr uint32_t kOperandBytes = 4u * kAtomBytes;     // 64 KB
+constexpr uint32_t kWeightBytes = kOperandBytes;
+
+// Byte offset of element (row r, k) in the 128-byte-swizzled K-major layout:
+// K atom k / 64, row r at 128 bytes, 16-byte chunk (k % 64) / 8 stored at
+// chunk ^ (r % 8).
+__host__ __device__ __forceinline__ uint32_t sw128_offset(int r, int k) {
+    const int atom = k >> 6, kk = k & 63;
+    return (uint32_t)atom * kAtomBytes + (uint32_t)r * 128u +
+           (uint32_t)((((kk >> 3) ^ (r & 7)) << 4) | ((kk & 7) << 1));
+}
+
+__global__ void enc_pack_weights_kernel(const float* __restrict__ w, int ci,
+                                        __half* __restrict__ img) {
+    const int idx = blockIdx.x * blockDim.x + threadIdx.x;  // co * kEncK + k
+    if (idx >= kEncCo * kEncK) return;
+    const int co = idx / kEncK, k = idx % kEncK;
+    const float v = k < ci ? w[co * ci + k] : 0.0f;
+    img[sw128_offset(co, k) / 2] = __float2half_rn(v);
+}
+
+struct EncParams {
+    const float* corr;  // [M][ci][hw]
+    const uint4* wimg;  // packed weights (kWeightBytes)
+    const float* bias;  // [128]
+    __half* out;        // [M][128][hw]
+    int* err;
+    int M, ci, hw;
+};
+
+__global__ void __launch_bounds__(kEncThreads, 1) corr_encoder_kernel(EncParams P) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    uint8_t* sB = base;                    // weights
+    uint8_t* sA = base + kWeightBytes;     // pixel tile
+    uint64_t* bar = reinterpret_cast<uint64_t*>(sA + kOperandBytes);
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 1);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int hw = P.hw;
+    const int tpe = (hw + kEncM - 1) / kEncM;
+    const int ntiles = tpe * P.M;
+
+    // resident weights (L2 -> shared, 16-byte loads)
+    for (int i = tid; i < (int)(kWeightBytes / 16); i += kEncThreads)
+        reinterpret_cast<uint4*>(sB)[i] = __ldg(P.wimg + i);
+    if (tid == 0) {
+        mbar_init(smem_addr(bar), 1);
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(smem_addr(tslot), 128);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+    const uint32_t idesc = idesc_f16(0u, kEncM, kEncCo);
+    const uint32_t aA = smem_addr(sA), aB = smem_addr(sB);
+    int phase = 0;
+    bool alive = true;
+
+    for (int t = blockIdx.x; t < ntiles && alive; t += gridDim.x, phase ^= 1) {
+        const int e = t / tpe, p0 = (t - e * tpe) * kEncM;
+        const int p = p0 + tid;
+        const bool pv = p < hw;
+        // A tile: row tid = pixel p, 8 channels per 16-byte chunk
+        const float* src = P.corr + (size_t)e * P.ci * hw + p;
+#pragma unroll 2
+        for (int c = 0; c < kEncK / 8; c++) {
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const int k = 8 * c + j;
+                v[j] = (pv && k < P.ci) ? __ldcs(src + (size_t)k * hw) : 0.0f;
+            }
+            uint4 pk;
+            __half2 h0 = __floats2half2_rn(v[0], v[1]), h1 = __floats2half2_rn(v[2], v[3]);
+            __half2 h2 = __floats2half2_rn(v[4], v[5]), h3 = __floats2half2_rn(v[6], v[7]);
+            pk.x = *reinterpret_cast<uint32_t*>(&h0);
+            pk.y = *reinterpret_cast<uint32_t*>(&h1);
+            pk.z = *reinterpret_cast<uint32_t*>(&h2);
+            pk.w = *reinterpret_cast<uint32_t*>(&h3);
+            *reinterpret_cast<uint4*>(sA + sw128_offset(tid, 8 * c)) = pk;
+        }
+        fence_proxy_async();  // generic-proxy stores -> tensor-core reads
+        tc_fence_before();
+        __syncthreads();
+        if (tid == 0) {
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < kEncK / 16; kk++) {
+                const int at = kk >> 2, wi = kk & 3;
+                mma_f16(tmem, sdesc_sw128(aA + at * kAtomBytes + wi * 32),
+                        sdesc_sw128(aB + at * kAtomBytes + wi * 32), idesc, kk > 0 ? 1u : 0u);
+            }
+            mma_commit(smem_addr(bar));
+        }
+        __syncwarp();
+        int ok = 1;
+        if (lane == 0) ok = mbar_wait(smem_addr(bar), phase, nullptr) ? 1 : 0;
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (ok) mbar_wait(smem_addr(bar), phase, nullptr);
+        if (!ok) {
+            if (lane == 0) atomicExch(P.err, 20);
+            alive = false;
+        }
+        // every warp must reach the barrier below, whether or not it gave up
+        if (alive) {
+            tc_fence_after();
+            const uint32_t tl = tmem + ((uint32_t)(32 * warp) << 16);
+            __half* o = P.out + (size_t)e * kEncCo * hw + p;
+#pragma unroll
+            for (int blk = 0; blk < kEncCo / 64; blk++) {
+                float acc[64];
+                tmem_ld64(tl + 64 * blk, acc);
+                if (pv) {
+#pragma unroll
+                    for (int j = 0; j < 64; j++) {
+                        const int co = 64 * blk + j;
+                        const float y = fmaxf(acc[j] + __ldg(P.bias + co), 0.0f);
+                        o[(size_t)co * hw] = __float2half_rn(y);
+                    }
+                }
+            }
+        }
+        tc_fence_before();
+        __syncthreads();
+        // a warp that timed out leaves the loop; so do the others (bar.sync
+        // above has collected every warp; the flag is re-read uniformly)
+        alive = __syncthreads_and(alive ? 1 : 0) != 0;
+    }
+    if (!alive && tid == 0) {
+        // the MMAs of the abandoned tile may still read shared memory: wait (bounded)
+        mbar_wait(smem_addr(bar), phase, nullptr);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 128);
+    }
+}
+
+}  // namespace
+
+int dc_set_corr_encoder_impl(dc_ctx* ctx, const float* weight, const float* bias, int co,
+                             cudaStream_t s) {
+    const int ci = ctx->cfg.levels * (2 * ctx->cfg.radius + 1) * (2 * ctx->cfg.radius + 1);
+    if (co != kEncCo)
+        return dc_fail(ctx, DC_ERR_UNSUPPORTED, "the correlation encoder has 128 output channels");
+    if (ci > kEncK)
+        return dc_fail(ctx, DC_ERR_UNSUPPORTED, "more than 256 correlation channels");
+    if (!ctx->enc_w) {
+        if (cudaMalloc(&ctx->enc_w, kWeightBytes + kEncCo * sizeof(float)) != cudaSuccess) {
+            cudaGetLastError();
+            ctx->enc_w = nullptr;
+            return dc_fail(ctx, DC_ERR_NO_MEMORY, "encoder weights");
+        }
+    }
+    float* b = reinterpret_cast<float*>(static_cast<char*>(ctx->enc_w) + kWeightBytes);
+    enc_pack_weights_kernel<<<(kEncCo * kEncK + 255) / 256, 256, 0, s>>>(
+        weight, ci, static_cast<__half*>(ctx->enc_w));
+    int rc = dc_check_launch(ctx, "enc_pack_weights_kernel");
+    if (rc) return rc;
+    if (cudaMemcpyAsync(b, bias, kEncCo * sizeof(float), cudaMemcpyDeviceToDevice, s) !=
+        cudaSuccess)
+        return dc_fail(ctx, DC_ERR_CUDA, "copying the encoder bias failed");
+    ctx->enc_ready = true;
+    return DC_OK;
+}
+
+int dc_launch_encoder(dc_ctx* ctx, const float* corr, int M, void* out, cudaStream_t s) {
+    if (!ctx->enc_ready)
+        return dc_fail(ctx, DC_ERR_NOT_READY, "dc_set_corr_encoder has not been called");
+    EncParams P;
+    P.corr = corr;
+    P.wimg = static_cast<const uint4*>(ctx->enc_w);
+    P.bias = reinterpret_cast<const float*>(static_cast<char*>(ctx->enc_w) + kWeightBytes);
+    P.out = static_cast<__half*>(out);
+    P.err = ctx->dev_err;
+    P.M = M;
+    P.ci = ctx->cfg.levels * (2 * ctx->cfg.radius + 1) * (2 * ctx->cfg.radius + 1);
+    P.hw = ctx->hw;
+    const size_t smem = 2 * kOperandBytes + 64 + 1024;
+    const int ntiles = (ctx->hw + kEncM - 1) / kEncM * M;
+    const int grid = ntiles < ctx->num_sms ? ntiles : ctx->num_sms;
+    cudaFuncSetAttribute(corr_encoder_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
+    corr_encoder_kernel<<<grid, kEncThreads, smem, s>>>(P);
+    return dc_check_launch(ctx, "corr_encoder_kernel");
+}

@@ -43,6 +43,9 @@ struct dc_ctx {
     // 4 target rows x 8 target columns x 64 channels (the fused kernel's B boxes)
     alignas(64) unsigned char tmap_b[DC_MAX_LEVELS][128];
     bool tc_ready = false;
+    // correlation encoder (dc_set_corr_encoder): packed fp16 weights, then the bias
+    void* enc_w = nullptr;
+    bool enc_ready = false;
     std::string err;
 };
 
@@ -144,5 +147,8 @@ int dc_scatter_mean_impl(dc_ctx* ctx, const float* feats, long long F, const int
                          int E, float* agg, int* kf_ids_host, int* K_out, cudaStream_t s);
 int dc_gather_rows_impl(dc_ctx* ctx, const float* src, long long F, int num_rows, const int* idx,
                         int n, float* dst, cudaStream_t s);
+int dc_set_corr_encoder_impl(dc_ctx* ctx, const float* weight, const float* bias, int co,
+                             cudaStream_t s);
+int dc_launch_encoder(dc_ctx* ctx, const float* corr, int M, void* out, cudaStream_t s);
 int dc_launch_alt(dc_ctx* ctx, const int* ii, const int* jj, int M, const float* coords,
                   float* out, cudaStream_t s);
