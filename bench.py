@@ -314,7 +314,7 @@ def main():
     # ---- per step (frontend workloads): keyframe f = k % frames arrives; rank 0
     # packs it into the ring's spare slot and broadcasts that slot, while the
     # step's kernel runs on the previous mapping; edges are translated to slots
-    n_steps_all = max(args.warmup, 3) + args.steps + 3 + 3 + args.steps + 2
+    n_steps_all = max(args.warmup, 3) + args.steps + 2 * (3 + args.steps) + 2
     step_edges = []
     ring_sim = SlotRing(wl.frames)
     for k in range(n_steps_all):
@@ -465,7 +465,10 @@ def main():
     s_h2d, s_comp, s_d2h = (torch.cuda.Stream(dev) for _ in range(3))
     bufs = [dict(fm=torch.empty_like(fm[:1]), coords=torch.empty_like(coords),
                  ii=torch.empty_like(ii_static), jj=torch.empty_like(jj_static),
-                 out=torch.empty_like(out)) for _ in range(2)]
+                 out=torch.empty_like(out),
+                 enc=torch.empty(M, 128, wl.h, wl.w, dtype=torch.float16, device=dev))
+            for _ in range(2)]
+    enc_h = torch.empty(M, 128, wl.h, wl.w, dtype=torch.float16).pin_memory()
     bounds = [(M * c // E2E_CHUNKS, M * (c + 1) // E2E_CHUNKS) for c in range(E2E_CHUNKS)]
     bounds = [(a, b) for a, b in bounds if b > a] if pipelined else [(0, M)]
     ev_in = [torch.cuda.Event() for _ in range(2)]
@@ -473,7 +476,7 @@ def main():
     ev_free = [torch.cuda.Event() for _ in range(2)]
     ev_chunk = [[torch.cuda.Event() for _ in bounds] for _ in range(2)]
 
-    def e2e_pipe_step(j):
+    def e2e_pipe_step(j, encode=False):
         nonlocal k_glob
         k = k_glob
         k_glob += 1
@@ -495,7 +498,11 @@ def main():
             if frontend:
                 prep(k, s_comp, fm_src=B["fm"])
             for c, (a0, a1) in enumerate(bounds):
-                if pipelined:
+                if encode:
+                    dc.build_lookup_encode(B["ii"][a0:a1], B["jj"][a0:a1], B["coords"][a0:a1],
+                                           corr=B["out"][a0:a1], out=B["enc"][a0:a1],
+                                           stream=s_comp)
+                elif pipelined:
                     dc.build_and_lookup(B["ii"][a0:a1], B["jj"][a0:a1], B["coords"][a0:a1],
                                         out=B["out"][a0:a1], stream=s_comp)
                 else:
@@ -506,29 +513,36 @@ def main():
         with torch.cuda.stream(s_d2h):
             for c, (a0, a1) in enumerate(bounds):
                 s_d2h.wait_event(ev_chunk[b][c])
-                out_h[a0:a1].copy_(B["out"][a0:a1], non_blocking=True)
+                if encode:
+                    enc_h[a0:a1].copy_(B["enc"][a0:a1], non_blocking=True)
+                else:
+                    out_h[a0:a1].copy_(B["out"][a0:a1], non_blocking=True)
             ev_free[b].record(s_d2h)
 
-    torch.cuda.synchronize()
-    for j in range(3):
-        e2e_pipe_step(j)
-    torch.cuda.synchronize()
-    if pg is not None:
-        pg.barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(s_h2d):
-        torch.cuda._sleep(int(0.02 * 1.9e9))
-    e0.record(s_h2d)
-    for j in range(args.steps):
-        e2e_pipe_step(3 + j)
-    e1.record(s_d2h)
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / args.steps
-    if pg is not None:
-        t = torch.tensor([e2e_ms], device=dev)
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        e2e_ms = t.item()
+    def time_e2e(encode):
+        torch.cuda.synchronize()
+        for j in range(3):
+            e2e_pipe_step(j, encode)
+        torch.cuda.synchronize()
+        if pg is not None:
+            pg.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(s_h2d):
+            torch.cuda._sleep(int(0.02 * 1.9e9))
+        e0.record(s_h2d)
+        for j in range(args.steps):
+            e2e_pipe_step(3 + j, encode)
+        e1.record(s_d2h)
+        torch.cuda.synchronize()
+        t_ms = e0.elapsed_time(e1) / args.steps
+        if pg is not None:
+            t = torch.tensor([t_ms], device=dev)
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+            t_ms = t.item()
+        return t_ms
+
+    e2e_ms = time_e2e(False)
     h2d = ((fm_h[0].numel() * 4 if frontend else 0) + coords_h.numel() * 4 + 2 * M * 4)
     d2h = out_h.numel() * 4
 
@@ -543,6 +557,31 @@ def main():
         assert torch.isfinite(chk).all().item()
         if pipelined:
             assert torch.equal(out_h, chk.cpu())
+
+    # ---- the same steps with the update operator's first corr-encoder layer
+    # fused behind the lookup (dc_build_lookup_encode: corr_enc_0 + ReLU + fp16,
+    # cuda_slam/main.cu:603-606, seeded weights): 128 fp16 channels go back
+    # to the host instead of 196 fp32 ones
+    e2e_enc = None
+    if pipelined and frontend and dc.out_channels <= 256:
+        wg = torch.Generator(device=dev)
+        wg.manual_seed(configs.SEED + 17)
+        enc_w = torch.randn(128, dc.out_channels, generator=wg, device=dev) / dc.out_channels ** 0.5
+        enc_b = 0.1 * torch.randn(128, generator=wg, device=dev)
+        dc.set_corr_encoder(enc_w, enc_b)
+        enc_ms = time_e2e(True)
+        if rank == 0:
+            last = bufs[(3 + args.steps - 1) % 2]
+            chk16, _ = dc.build_lookup_encode(last["ii"], last["jj"], last["coords"])
+            torch.cuda.synchronize()
+            assert torch.equal(enc_h, chk16.cpu())
+        e2e_enc = {"value": M * world / (enc_ms * 1e-3), "unit": UNIT,
+                   "h2d_bytes_per_step": ((fm_h[0].numel() * 4 if rank == 0 else 0)
+                                          + coords_h.numel() * 4 + 2 * M * 4),
+                   "d2h_bytes_per_step": enc_h.numel() * 2, "ms_per_step": enc_ms,
+                   "what": "each step also encodes the 196 correlation channels to the "
+                           "update operator's 128 fp16 channels on the GPU "
+                           "(dc_build_lookup_encode) and copies those out"}
 
     if rank != 0:
         if pg is not None:
@@ -634,6 +673,8 @@ def main():
         line["stages"] = stages
     if replication is not None:
         line["replication"] = replication
+    if e2e_enc is not None:
+        line["e2e_encoded"] = e2e_enc
 
     # reference kernels on this GPU (cuBLAS FP16 GEMM + pools + lookups), if built
     if not args.no_ref_gpu and world == 1:
