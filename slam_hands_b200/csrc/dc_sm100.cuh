@@ -30,18 +30,18 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
                  : "memory");
 }
-// Longest time (ns) one try_wait may keep the thread suspended: the thread
-// resumes as soon as the phase completes, so a long hint only saves the issue
-// slots of repeated polls.
-constexpr uint32_t kSuspendHintNs = 20000;
+// One poll of a barrier phase: mbarrier.test_wait never suspends the thread,
+// so a waiting role sees the phase flip as soon as it happens (measured: a
+// try_wait with a 20 us suspend hint made the fused kernel 2-5 % slower, its
+// pipeline hand-offs alone 25 % slower).
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(bar), "r"(parity), "r"(kSuspendHintNs)
+        : "r"(bar), "r"(parity)
         : "memory");
     return ok != 0;
 }
@@ -55,8 +55,7 @@ __device__ __forceinline__ uint64_t globaltimer() {
 // Wait for phase `parity` of a barrier, giving up after `limit_ns` or when
 // *abort (if given) becomes non-zero.  Returns false on give-up (the caller records the
 // failure and leaves its loop); no wait in the library is unbounded.
-// mbarrier.try_wait itself suspends the thread for a hardware time window, so
-// the loop polls without sleeping (a sleep would add its whole length to every
+// The loop polls without sleeping (a sleep would add its whole length to every
 // hand-off between pipeline roles); only a wait already longer than 50 us backs
 // off with __nanosleep, and the abort flag and the clock are read every 64 polls.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
