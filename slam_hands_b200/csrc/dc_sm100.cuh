@@ -76,6 +76,18 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
     }
 }
 
+// 16-byte shared-memory store under a predicate, without a branch (a branch per
+// optional store diverges and reconverges the warp).
+__device__ __forceinline__ void st_shared_v4_if(bool pred, uint32_t addr, float a, float b,
+                                                float c, float d) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.u32 p, %0, 0;\n\t"
+        "@p st.shared.v4.f32 [%1], {%2, %3, %4, %5};\n\t}" ::"r"((uint32_t)pred),
+        "r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+        : "memory");
+}
+
 // ---- TMA ---------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");

@@ -50,17 +50,23 @@ namespace {
 using namespace dc::sm100;
 
 constexpr int kTileM = 128;      // source pixels per CTA = MMA M = TMEM lanes
-constexpr int kChunkN = 256;     // max targets per chunk = MMA N
+#ifndef DC_TC_CHUNKN
+#define DC_TC_CHUNKN 256
+#endif
+#ifndef DC_TC_STAGES_B
+#define DC_TC_STAGES_B 2
+#endif
+constexpr int kChunkN = DC_TC_CHUNKN;  // max targets per chunk = MMA N
 constexpr int kStrip = 8;        // target pixels per strip
 constexpr int kChunkStrips = kChunkN / kStrip;  // 32 strips per chunk
-constexpr int kStagesB = 2;      // shared-memory stages of target rows
-constexpr int kAcc = 2;          // TMEM accumulators
-constexpr int kAccCols = 256;    // TMEM columns per accumulator
+constexpr int kStagesB = DC_TC_STAGES_B;  // shared-memory stages of target rows
+constexpr int kAccCols = kChunkN;         // TMEM columns per accumulator
+constexpr int kAcc = 512 / kAccCols;      // TMEM accumulators
 #ifndef DC_TC_SUBWARPS
 #define DC_TC_SUBWARPS 2
 #endif
 constexpr int kSubWarps = DC_TC_SUBWARPS;  // epilogue warps per TMEM lane quarter
-constexpr int kWarpBlocks = 4 / kSubWarps;   // 64-column blocks per epilogue warp and chunk
+constexpr int kWarpBlocks = kChunkN / 64 / kSubWarps;  // 64-column blocks per epilogue warp and chunk
 constexpr int kEpiWarps = 4 * kSubWarps;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kWinRow = 16;      // floats per window row: two 8-column strip slots
@@ -71,8 +77,9 @@ constexpr int kWinStride = 8 * kWinRow;      // floats per pixel
 constexpr uint32_t kTmemCols = kAcc * kAccCols;
 constexpr uint32_t kRowBytes = 128;  // one 128-byte K atom per operand row
 static_assert(kChunkN <= kAccCols && kChunkN % 16 == 0, "MMA N");
-static_assert(kChunkStrips == 32, "one bit per strip of a chunk");
-static_assert(kSubWarps == 2 || kSubWarps == 4, "a chunk is four 64-column blocks");
+static_assert(kChunkStrips <= 32, "one bit per strip of a chunk");
+static_assert(kWarpBlocks >= 1, "every epilogue warp drains at least one 64-column block");
+static_assert(kSubWarps == 2 || kSubWarps == 4, "epilogue warps per lane quarter");
 
 // Per-level constants of the target boxes (host-computed): a box holds br rows
 // of wbox pixels (wbox a multiple of 8, br * wbox <= 256); a row wider than
@@ -351,7 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int l = idx / (kChunkStrips + 1), r = idx % (kChunkStrips + 1);
         const int spr = P.box[l].wbox / kStrip;
         unsigned m = 0;
-        for (int i = 0; i < r && i * spr < 32; i++) m |= 1u << (i * spr);
+        for (int i = 0; i < r && i * spr < kChunkStrips; i++) m |= 1u << (i * spr);
         rep_tab[idx] = m;
     }
     tc_fence_before();
@@ -613,6 +620,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int sub = (warp - 2) >> 2;    // which loads / output columns (0..kSubWarps-1)
         const int ti_px = 32 * quarter + lane;
         float* win = win_base + ti_px * kWinStride;
+        const uint32_t win_s = smem_addr(win);
         const int swz = ti_px & 3;  // unit swizzle of this pixel's window rows
         const uint32_t tl = tmem + ((uint32_t)(32 * quarter) << 16);
         int gc = 0, i = 0;
@@ -701,16 +709,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (lane == 0 && warp == 2) DC_TRACE(5 + bb, gc);
 #pragma unroll
                         for (int k = 0; k < 8; k++) {
-                            if (n8 & (1u << k)) {
-                                const int e = strip_l[8 * blk + k];
-                                const int wr = ry + (e & 0xffff);
-                                const int u = 2 * ((e >> 16) - xs0);
-                                float4* d4 = reinterpret_cast<float4*>(win + wr * kWinRow);
-                                d4[u ^ swz] = make_float4(v[8 * k + 0], v[8 * k + 1],
-                                                          v[8 * k + 2], v[8 * k + 3]);
-                                d4[(u + 1) ^ swz] = make_float4(v[8 * k + 4], v[8 * k + 5],
-                                                                v[8 * k + 6], v[8 * k + 7]);
-                            }
+                            // predicated stores: no per-strip branch
+                            const bool need = (n8 >> k) & 1u;
+                            const int e = strip_l[8 * blk + k];
+                            const int wr = ry + (e & 0xffff);
+                            const int u = 2 * ((e >> 16) - xs0);
+                            const uint32_t row = win_s + (uint32_t)(wr * kWinRow) * 4u;
+                            st_shared_v4_if(need, row + (uint32_t)((u ^ swz) << 4), v[8 * k + 0],
+                                            v[8 * k + 1], v[8 * k + 2], v[8 * k + 3]);
+                            st_shared_v4_if(need, row + (uint32_t)(((u + 1) ^ swz) << 4),
+                                            v[8 * k + 4], v[8 * k + 5], v[8 * k + 6],
+                                            v[8 * k + 7]);
                         }
                     }
                     tc_fence_before();
