@@ -53,7 +53,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="C2")
-    ap.add_argument("--precision", default="fp16", choices=["fp32", "tf32", "bf16", "fp16"])
+    ap.add_argument("--precision", default="fp16", choices=["fp32", "tf32", "bf16", "fp16", "fp32x3"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-gpu", action="store_true")
     ap.add_argument("--scatter-mean", action="store_true",
@@ -591,7 +591,7 @@ def main():
     # ---- roofline of the dominant kernel (algorithmic bytes per launch / event time)
     hw = wl.h * wl.w
     D = 2 * dc.radius + 1
-    esz = 2 if args.precision in ("fp16", "bf16") else 4
+    esz = 4 if args.precision in ("fp32", "fp32x3") else 2  # fp32x3: hi + lo fp16 copies
     uniq_frames = len(set(ii) | set(jj))
     pyr_rows = sum((wl.h >> l) * (wl.w >> l) for l in range(dc.levels))
     io_bytes = M * (2 * hw * 4 + dc.out_channels * hw * 4)          # coords in, output out
@@ -626,8 +626,8 @@ def main():
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "kernel": kernel_name, "peak_source": peak_src,
                 "alg_bytes_per_launch": alg_bytes}
-    if vols is None and proj is None and args.precision in ("fp32", "tf32"):
-        # exact / TF32-rounded modes run the alt-corr kernel: FP32 CUDA-core work,
+    if vols is None and proj is None and args.precision == "fp32":
+        # the exact mode runs the alt-corr kernel: FP32 CUDA-core work,
         # (2r+2)^2 taps x 2C flops per pixel and level (windows not clipped at borders)
         flops = M * hw * dc.levels * (2 * dc.radius + 2) ** 2 * 2 * wl.channels
         fp32_peak = 148 * 128 * 2 * 1.965e9 / 1e12  # SMs x FP32 lanes x FMA x max clock

@@ -65,16 +65,30 @@ typedef struct dc_ctx dc_ctx;
 #define DC_ERR_NOT_READY 6
 
 /* Arithmetic of the correlation dot products (the volume build).
- *   DC_PREC_FP32  exact fp32 FFMA, channels accumulated in order c = 0..C-1
- *   DC_PREC_TF32  inputs rounded to TF32, fp32 accumulate (tensor cores)
- *   DC_PREC_BF16  inputs rounded to BF16, fp32 accumulate (tensor cores)
- *   DC_PREC_FP16  inputs rounded to FP16, fp32 accumulate (tensor cores) --
- *                 the reference's own arithmetic (FP16 fmaps, cublasGemmBatchedEx
- *                 with CUBLAS_COMPUTE_32F, main.cu:1573-1581). */
+ *   DC_PREC_FP32    exact fp32 FFMA, channels accumulated in order c = 0..C-1
+ *                   (CUDA cores; bit-exact materialised volume)
+ *   DC_PREC_TF32    inputs rounded to TF32 (10 explicit mantissa bits, round to
+ *                   nearest, ties away), fp32 accumulate on the tensor cores: a
+ *                   TF32 value within fp16's normal range (2^-14 <= |x| < 65504)
+ *                   is an fp16 value, so the store holds fp16 and the fp16
+ *                   kernels run; smaller magnitudes keep fp16's (subnormal)
+ *                   precision
+ *   DC_PREC_BF16    inputs rounded to BF16, fp32 accumulate (tensor cores)
+ *   DC_PREC_FP16    inputs rounded to FP16, fp32 accumulate (tensor cores) --
+ *                   the reference's own arithmetic (FP16 fmaps, cublasGemmBatchedEx
+ *                   with CUBLAS_COMPUTE_32F, main.cu:1573-1581)
+ *   DC_PREC_FP32X3  fp32 accuracy on the tensor cores: every input is split into
+ *                   hi = fp16(x) and lo = fp16(x - hi), and each dot product is
+ *                   hi.hi + hi.lo + lo.hi (three fp16 passes, fp32 accumulation;
+ *                   the dropped lo.lo term is ~2^-22 relative) -- within 1e-5 of
+ *                   the fp32 result for inputs within fp16's range.  Serves
+ *                   dc_build_and_lookup (and dc_project_build_and_lookup) only;
+ *                   channels 64 or 128. */
 #define DC_PREC_FP32 0
 #define DC_PREC_TF32 1
 #define DC_PREC_BF16 2
 #define DC_PREC_FP16 3
+#define DC_PREC_FP32X3 4
 
 /* element type of caller feature maps */
 #define DC_DTYPE_F32 0

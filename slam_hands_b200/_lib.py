@@ -27,8 +27,9 @@ DC_PREC_FP32 = 0
 DC_PREC_TF32 = 1
 DC_PREC_BF16 = 2
 DC_PREC_FP16 = 3
+DC_PREC_FP32X3 = 4
 PRECISIONS = {"fp32": DC_PREC_FP32, "tf32": DC_PREC_TF32, "bf16": DC_PREC_BF16,
-              "fp16": DC_PREC_FP16}
+              "fp16": DC_PREC_FP16, "fp32x3": DC_PREC_FP32X3}
 
 DC_DTYPE_F32 = 0
 DC_DTYPE_F16 = 1

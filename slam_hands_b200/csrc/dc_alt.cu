@@ -187,7 +187,9 @@ int launch_c(dc_ctx* ctx, const int* ii, const int* jj, int M, const float* coor
 int dc_launch_alt(dc_ctx* ctx, const int* ii, const int* jj, int M, const float* coords,
                   float* out, cudaStream_t s) {
     switch (ctx->cfg.precision) {
-        case DC_PREC_FP16: return launch_c<__half>(ctx, ii, jj, M, coords, out, s);
+        case DC_PREC_FP16:
+        case DC_PREC_TF32:  // TF32-rounded values held as fp16
+            return launch_c<__half>(ctx, ii, jj, M, coords, out, s);
         case DC_PREC_BF16: return launch_c<__nv_bfloat16>(ctx, ii, jj, M, coords, out, s);
         default: return launch_c<float>(ctx, ii, jj, M, coords, out, s);
     }

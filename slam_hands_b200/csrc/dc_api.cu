@@ -32,6 +32,36 @@ int validate_edges(dc_ctx* ctx, const int* ii, const int* jj, int M) {
 
 }  // namespace
 
+int dc_init_geometry(dc_ctx* ctx, const dc_config& c, int frames) {
+    if (c.h < 1 || c.w < 1 || (long long)c.h * c.w > DC_MAX_HW) return DC_ERR_INVALID_ARG;
+    if (c.channels != 32 && c.channels != 64 && c.channels != 128 && c.channels != 256)
+        return DC_ERR_INVALID_ARG;
+    if (c.levels < 1 || c.levels > DC_MAX_LEVELS) return DC_ERR_INVALID_ARG;
+    if (c.radius < 0 || c.radius > DC_MAX_RADIUS) return DC_ERR_INVALID_ARG;
+    if (c.precision < DC_PREC_FP32 || c.precision > DC_PREC_FP32X3) return DC_ERR_INVALID_ARG;
+    if (c.precision == DC_PREC_FP32X3 && c.channels != 64 && c.channels != 128)
+        return DC_ERR_INVALID_ARG;
+    if ((c.h >> (c.levels - 1)) < 1 || (c.w >> (c.levels - 1)) < 1) return DC_ERR_INVALID_ARG;
+    ctx->cfg = c;
+    ctx->hw = c.h * c.w;
+    long long rows = 0;
+    for (int l = 0; l < DC_MAX_LEVELS; l++) {
+        ctx->H[l] = c.h >> l;
+        ctx->W[l] = c.w >> l;
+        ctx->level_row0[l] = rows;
+        if (l < c.levels) {
+            long long n = (long long)ctx->H[l] * ctx->W[l];
+            rows += (n + DC_ROW_PAD - 1) / DC_ROW_PAD * DC_ROW_PAD;
+        }
+    }
+    // FP32X3 keeps a lo copy of every slot right after its hi rows
+    ctx->lo_rows = c.precision == DC_PREC_FP32X3 ? rows : 0;
+    ctx->frame_rows = c.precision == DC_PREC_FP32X3 ? 2 * rows : rows;
+    ctx->elem_bytes = dc_store_is_16bit(c.precision) ? 2 : 4;
+    ctx->store_bytes = (long long)frames * ctx->frame_rows * c.channels * ctx->elem_bytes;
+    return DC_OK;
+}
+
 extern "C" {
 
 void dc_default_config(dc_config* cfg, int h, int w) {
@@ -63,36 +93,17 @@ int dc_create(const dc_config* cfg, dc_ctx** out) {
     if (!cfg || !out) return DC_ERR_INVALID_ARG;
     *out = nullptr;
     const dc_config& c = *cfg;
-    if (c.h < 1 || c.w < 1 || (long long)c.h * c.w > DC_MAX_HW) return DC_ERR_INVALID_ARG;
-    if (c.channels != 32 && c.channels != 64 && c.channels != 128 && c.channels != 256)
-        return DC_ERR_INVALID_ARG;
-    if (c.levels < 1 || c.levels > DC_MAX_LEVELS) return DC_ERR_INVALID_ARG;
-    if (c.radius < 0 || c.radius > DC_MAX_RADIUS) return DC_ERR_INVALID_ARG;
     if (c.max_frames < 1 || c.max_edges < 1) return DC_ERR_INVALID_ARG;
-    if (c.precision < DC_PREC_FP32 || c.precision > DC_PREC_FP16) return DC_ERR_INVALID_ARG;
-    if ((c.h >> (c.levels - 1)) < 1 || (c.w >> (c.levels - 1)) < 1) return DC_ERR_INVALID_ARG;
-
     dc_ctx* ctx = new dc_ctx();
-    ctx->cfg = c;
+    if (dc_init_geometry(ctx, c, c.max_frames) != DC_OK) {
+        delete ctx;
+        return DC_ERR_INVALID_ARG;
+    }
     if (cudaGetDevice(&ctx->device) != cudaSuccess) {
         delete ctx;
         return DC_ERR_CUDA;
     }
     cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, ctx->device);
-    ctx->hw = c.h * c.w;
-    long long rows = 0;
-    for (int l = 0; l < DC_MAX_LEVELS; l++) {
-        ctx->H[l] = c.h >> l;
-        ctx->W[l] = c.w >> l;
-        ctx->level_row0[l] = rows;
-        if (l < c.levels) {
-            long long n = (long long)ctx->H[l] * ctx->W[l];
-            rows += (n + DC_ROW_PAD - 1) / DC_ROW_PAD * DC_ROW_PAD;
-        }
-    }
-    ctx->frame_rows = rows;
-    ctx->elem_bytes = (c.precision == DC_PREC_FP16 || c.precision == DC_PREC_BF16) ? 2 : 4;
-    ctx->store_bytes = (long long)c.max_frames * rows * c.channels * ctx->elem_bytes;
     if (cudaMalloc(&ctx->store, ctx->store_bytes) != cudaSuccess) {
         cudaGetLastError();
         delete ctx;
@@ -182,6 +193,8 @@ int dc_build_volume(dc_ctx* ctx, const int* ii, const int* jj, int M, float* con
     int rc = validate_edges(ctx, ii, jj, M);
     if (rc) return rc;
     if (!vols || !vols[0]) return dc_fail(ctx, DC_ERR_INVALID_ARG, "vols[0] is NULL");
+    if (ctx->cfg.precision == DC_PREC_FP32X3)
+        return dc_fail(ctx, DC_ERR_UNSUPPORTED, "DC_PREC_FP32X3 serves the fused lookup only");
     if (M == 0) return DC_OK;
     rc = ctx->tc_ready ? dc_launch_volume_tc(ctx, ii, jj, M, vols[0], (cudaStream_t)stream)
                        : dc_launch_volume_ffma(ctx, ii, jj, M, vols[0], (cudaStream_t)stream);
@@ -234,6 +247,8 @@ int dc_alt_lookup(dc_ctx* ctx, const int* ii, const int* jj, int M, const float*
     if (rc) return rc;
     if (M == 0) return DC_OK;
     if (!coords || !out) return dc_fail(ctx, DC_ERR_INVALID_ARG, "NULL pointer");
+    if (ctx->cfg.precision == DC_PREC_FP32X3)
+        return dc_fail(ctx, DC_ERR_UNSUPPORTED, "DC_PREC_FP32X3 serves the fused lookup only");
     return dc_launch_alt(ctx, ii, jj, M, coords, out, (cudaStream_t)stream);
 }
 

@@ -29,6 +29,7 @@ struct dc_ctx {
     int H[DC_MAX_LEVELS] = {0}, W[DC_MAX_LEVELS] = {0};
     long long level_row0[DC_MAX_LEVELS] = {0};
     long long frame_rows = 0;
+    long long lo_rows = 0;  // DC_PREC_FP32X3: a slot holds hi rows, then the lo copy at +lo_rows
     int elem_bytes = 4;
     void* store = nullptr;  // device
     long long store_bytes = 0;
@@ -42,6 +43,7 @@ struct dc_ctx {
     // per level, a 4-D map [slot][H_l][W_l][C] of the same store with boxes of
     // 4 target rows x 8 target columns x 64 channels (the fused kernel's B boxes)
     alignas(64) unsigned char tmap_b[DC_MAX_LEVELS][128];
+    alignas(64) unsigned char tmap_b_lo[DC_MAX_LEVELS][128];  // DC_PREC_FP32X3: the lo copy
     bool tc_ready = false;
     // correlation encoder (dc_set_corr_encoder): packed fp16 weights, then the bias
     void* enc_w = nullptr;
@@ -57,6 +59,7 @@ struct Geom {
     int H[DC_MAX_LEVELS], W[DC_MAX_LEVELS];
     long long row0[DC_MAX_LEVELS];
     long long frame_rows;
+    long long lo_rows;
     float alpha;
 };
 
@@ -74,6 +77,7 @@ inline Geom geom_of(const dc_ctx* c) {
         g.row0[l] = c->level_row0[l];
     }
     g.frame_rows = c->frame_rows;
+    g.lo_rows = c->lo_rows;
     g.alpha = c->cfg.alpha;
     return g;
 }
@@ -118,6 +122,14 @@ __device__ __forceinline__ float bilinear_tap(float acc, float s, bool valid, fl
 }
 
 }  // namespace dc
+
+// Validate a configuration and fill the context's geometry (levels, store rows,
+// element size, store bytes for `frames` slots).  Returns DC_OK or
+// DC_ERR_INVALID_ARG.
+int dc_init_geometry(dc_ctx* ctx, const dc_config& c, int frames);
+
+// Store element type of a precision: 16-bit for the tensor-core precisions.
+inline bool dc_store_is_16bit(int precision) { return precision != DC_PREC_FP32; }
 
 // Launch helpers: record the launch and turn launch errors into a status.
 int dc_fail(dc_ctx* ctx, int status, const std::string& msg);

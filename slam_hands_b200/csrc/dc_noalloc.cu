@@ -70,12 +70,6 @@ int dc_build_and_lookup_static(const dc_config* cfg, const void* fmaps, int dtyp
                                const float* coords, float* out, dc_stream_t stream) {
     if (!cfg) return fail(DC_ERR_INVALID_ARG, "cfg is NULL");
     const dc_config& c = *cfg;
-    if (c.h < 1 || c.w < 1 || (long long)c.h * c.w > DC_MAX_HW ||
-        (c.channels != 32 && c.channels != 64 && c.channels != 128 && c.channels != 256) ||
-        c.levels < 1 || c.levels > DC_MAX_LEVELS || c.radius < 0 || c.radius > DC_MAX_RADIUS ||
-        c.precision < DC_PREC_FP32 || c.precision > DC_PREC_FP16 ||
-        (c.h >> (c.levels - 1)) < 1 || (c.w >> (c.levels - 1)) < 1)
-        return fail(DC_ERR_INVALID_ARG, "invalid dc_config");
     if (dtype != DC_DTYPE_F32 && dtype != DC_DTYPE_F16)
         return fail(DC_ERR_INVALID_ARG, "dtype must be DC_DTYPE_F32 or DC_DTYPE_F16");
     if (num_frames < 1 || M < 0) return fail(DC_ERR_INVALID_ARG, "num_frames < 1 or M < 0");
@@ -84,21 +78,10 @@ int dc_build_and_lookup_static(const dc_config* cfg, const void* fmaps, int dtyp
 
     // the context a dc_create would build, on the stack, over the static store
     dc_ctx ctx;
-    ctx.cfg = c;
+    if (dc_init_geometry(&ctx, c, num_frames) != DC_OK)
+        return fail(DC_ERR_INVALID_ARG, "invalid dc_config");
     ctx.cfg.max_frames = num_frames;
     ctx.cfg.max_edges = M;
-    ctx.hw = c.h * c.w;
-    long long rows = 0;
-    for (int l = 0; l < DC_MAX_LEVELS; l++) {
-        ctx.H[l] = c.h >> l;
-        ctx.W[l] = c.w >> l;
-        ctx.level_row0[l] = rows;
-        if (l < c.levels)
-            rows += ((long long)ctx.H[l] * ctx.W[l] + DC_ROW_PAD - 1) / DC_ROW_PAD * DC_ROW_PAD;
-    }
-    ctx.frame_rows = rows;
-    ctx.elem_bytes = (c.precision == DC_PREC_FP16 || c.precision == DC_PREC_BF16) ? 2 : 4;
-    ctx.store_bytes = (long long)num_frames * rows * c.channels * ctx.elem_bytes;
     if (ctx.store_bytes > (long long)kScratchBytes) {
         char msg[200];
         std::snprintf(msg, sizeof msg,

@@ -16,16 +16,29 @@
 
 namespace {
 
+// Packing modes: the value itself, its TF32 rounding, or (FP32X3) the fp16
+// remainder x - fp16(x) for the lo copy.
+enum { kPackPlain = 0, kPackTf32 = 1, kPackSplit = 2 };
+
 template <typename T>
-__device__ __forceinline__ T pack_value(float v, bool tf32) {
-    if (tf32) v = dc::round_tf32(v);
+__device__ __forceinline__ T pack_value(float v, int mode) {
+    if (mode == kPackTf32) v = dc::round_tf32(v);
     return dc::from_f32<T>(v);
+}
+
+// Writes element v of a row: the row itself, and under kPackSplit also the lo
+// copy lo_off elements further (lo = fp16(x - fp16(x)), exact subtraction).
+template <typename T>
+__device__ __forceinline__ void put(T* dst, float v, int mode, long long lo_off) {
+    const T hi = pack_value<T>(v, mode);
+    dst[0] = hi;
+    if (mode == kPackSplit) dst[lo_off] = dc::from_f32<T>(v - dc::to_f32(hi));
 }
 
 template <typename Tin, typename T>
 __global__ void __launch_bounds__(256) store_pack_kernel(const Tin* __restrict__ fmaps,
                                                           T* __restrict__ store, dc::Geom g,
-                                                          int first, bool tf32) {
+                                                          int first, int mode) {
     extern __shared__ float sm[];
     // one CTA: one 8x8 tile of one slot, 32 of the C channels
     constexpr int C = 32, lc = 5;
@@ -43,6 +56,7 @@ __global__ void __launch_bounds__(256) store_pack_kernel(const Tin* __restrict__
     const int x0 = blockIdx.x * 8, y0 = blockIdx.y * 8;
     const Tin* f = fmaps + ((size_t)slot_local * CT + grp * C) * g.hw;
     T* st = store + (size_t)slot * g.frame_rows * CT + grp * C;
+    const long long lo_off = g.lo_rows * CT;
 
     // all loads of a thread in flight at once (8 per thread)
     static_assert(C * 64 % 256 == 0, "256 threads");
@@ -66,7 +80,7 @@ __global__ void __launch_bounds__(256) store_pack_kernel(const Tin* __restrict__
         int k = idx >> lc, c = idx & (C - 1);
         int y = y0 + (k >> 3), x = x0 + (k & 7);
         if (y < g.h && x < g.w)
-            st[(g.row0[0] + y * g.w + x) * CT + c] = pack_value<T>(t0[c * 65 + k], tf32);
+            put<T>(st + (g.row0[0] + y * g.w + x) * CT + c, t0[c * 65 + k], mode, lo_off);
     }
     // cascaded pooling inside the tile: level l has (8 >> l)^2 tile-local cells
     float* src = t0;
@@ -90,7 +104,8 @@ __global__ void __launch_bounds__(256) store_pack_kernel(const Tin* __restrict__
             int k = idx >> lc, c = idx & (C - 1);
             int y = gy0 + (k >> ld), x = gx0 + (k & (dw - 1));
             if (y < g.H[l] && x < g.W[l])
-                st[(g.row0[l] + y * g.W[l] + x) * CT + c] = pack_value<T>(dst[c * (dw * dw + (dw > 1)) + k], tf32);
+                put<T>(st + (g.row0[l] + y * g.W[l] + x) * CT + c, dst[c * (dw * dw + (dw > 1)) + k],
+                       mode, lo_off);
         }
         src = dst;
     }
@@ -103,8 +118,10 @@ int launch_store_t(dc_ctx* ctx, const void* fmaps, int first, int count, cudaStr
     size_t smem = (size_t)32 * (65 + 17 + 5 + 1) * sizeof(float);
     auto k = store_pack_kernel<Tin, T>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    k<<<grid, 256, smem, s>>>((const Tin*)fmaps, (T*)ctx->store, g, first,
-                              ctx->cfg.precision == DC_PREC_TF32);
+    const int mode = ctx->cfg.precision == DC_PREC_TF32    ? kPackTf32
+                     : ctx->cfg.precision == DC_PREC_FP32X3 ? kPackSplit
+                                                            : kPackPlain;
+    k<<<grid, 256, smem, s>>>((const Tin*)fmaps, (T*)ctx->store, g, first, mode);
     return dc_check_launch(ctx, "store_pack_kernel");
 }
 
@@ -118,7 +135,8 @@ __global__ void __launch_bounds__(256) store_zero_padding_kernel(uint4* __restri
     const int l = blockIdx.y, slot = first + blockIdx.x;
     const long long hw_l = (long long)g.H[l] * g.W[l];
     const long long rows_l = (hw_l + DC_ROW_PAD - 1) / DC_ROW_PAD * DC_ROW_PAD;
-    const long long r0 = (long long)slot * g.frame_rows + g.row0[l] + hw_l;
+    // blockIdx.z = 1: the lo copy of an FP32X3 slot
+    const long long r0 = (long long)slot * g.frame_rows + blockIdx.z * g.lo_rows + g.row0[l] + hw_l;
     const long long n16 = (rows_l - hw_l) * row_bytes / 16;
     uint4* p = store + r0 * row_bytes / 16;
     for (long long i = threadIdx.x; i < n16; i += blockDim.x) p[i] = make_uint4(0, 0, 0, 0);
@@ -128,7 +146,7 @@ __global__ void __launch_bounds__(256) store_zero_padding_kernel(uint4* __restri
 
 int dc_launch_store_zero_padding(dc_ctx* ctx, int first, int count, cudaStream_t s) {
     if (count <= 0) return DC_OK;
-    dim3 grid(count, ctx->cfg.levels);
+    dim3 grid(count, ctx->cfg.levels, ctx->lo_rows > 0 ? 2 : 1);
     store_zero_padding_kernel<<<grid, 256, 0, s>>>(static_cast<uint4*>(ctx->store),
                                                   dc::geom_of(ctx), first,
                                                   ctx->cfg.channels * ctx->elem_bytes);
@@ -138,12 +156,13 @@ int dc_launch_store_zero_padding(dc_ctx* ctx, int first, int count, cudaStream_t
 int dc_launch_store(dc_ctx* ctx, const void* fmaps, int dtype, int first, int count,
                     cudaStream_t s) {
     const int p = ctx->cfg.precision;
+    // store element: bf16 for BF16, fp32 for FP32, fp16 otherwise (FP16, TF32, FP32X3)
     if (dtype == DC_DTYPE_F32) {
-        if (p == DC_PREC_FP16) return launch_store_t<float, __half>(ctx, fmaps, first, count, s);
         if (p == DC_PREC_BF16) return launch_store_t<float, __nv_bfloat16>(ctx, fmaps, first, count, s);
-        return launch_store_t<float, float>(ctx, fmaps, first, count, s);
+        if (p == DC_PREC_FP32) return launch_store_t<float, float>(ctx, fmaps, first, count, s);
+        return launch_store_t<float, __half>(ctx, fmaps, first, count, s);
     }
-    if (p == DC_PREC_FP16) return launch_store_t<__half, __half>(ctx, fmaps, first, count, s);
     if (p == DC_PREC_BF16) return launch_store_t<__half, __nv_bfloat16>(ctx, fmaps, first, count, s);
-    return launch_store_t<__half, float>(ctx, fmaps, first, count, s);
+    if (p == DC_PREC_FP32) return launch_store_t<__half, float>(ctx, fmaps, first, count, s);
+    return launch_store_t<__half, __half>(ctx, fmaps, first, count, s);
 }

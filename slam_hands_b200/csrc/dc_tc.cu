@@ -145,6 +145,9 @@ struct TcParams {
     uint32_t ab_fmt;  // 0 fp16, 1 bf16
     int M;            // edges
     int stall;        // test hook: withhold each CTA's first source-tile load
+    long long a_off;  // source rows: 0 = the slot's (hi) rows, lo_rows = its lo copy (FP32X3)
+    int accum;        // add to `out` instead of writing it (FP32X3 passes 2 and 3)
+    int keep;         // a later pass reads `out` back: ordinary (L2-resident) stores
     unsigned long long wait_ns;  // limit of the pipeline waits (the drain waits keep 2 s)
 };
 
@@ -248,7 +251,9 @@ __device__ __forceinline__ void quarter_sync(int quarter) {
 template <int R, int AW, bool kCheck>
 __device__ __forceinline__ void bilinear_columns(const float* win, int swz, int kx, int a0, int bx,
                                                  int by, int Wl, int Hl, bool any, float dx,
-                                                 float dy, float alpha, float* ol, int hw) {
+                                                 float dy, float alpha, float* ol, int hw,
+                                                 bool accum, bool keep,
+                                                 const float (&old)[AW][2 * R + 1]) {
     constexpr int D = 2 * R + 1, NW = 2 * R + 2;
     bool vy[NW];
 #pragma unroll
@@ -279,13 +284,30 @@ __device__ __forceinline__ void bilinear_columns(const float* win, int swz, int 
                 acc = fmaf(pu[b + 1], dy, acc);
                 acc = fmaf(tap[b] * vx_w, uy, acc);
                 acc = fmaf(tap[b + 1] * vx_w, dy, acc);
-                __stcs(o, acc);
+                if (accum) acc = old[ii - 1][b] + acc;  // FP32X3 passes 2, 3 add their products
+                if (keep)
+                    *o = acc;  // read again by the next FP32X3 pass: keep it in L2
+                else
+                    __stcs(o, acc);
                 o += hw;
             }
         }
 #pragma unroll
         for (int j = 0; j < NW; j++) pu[j] = tap[j] * ux;
     }
+}
+
+// The outputs an FP32X3 pass adds to (columns a0 .. a0 + AW - 1), loaded before
+// the level's window barrier so that their latency hides behind it.
+template <int R, int AW>
+__device__ __forceinline__ void load_old(const float* ol, int a0, int hw,
+                                         float (&old)[AW][2 * R + 1]) {
+    constexpr int D = 2 * R + 1;
+#pragma unroll
+    for (int ii = 0; ii < AW; ii++)
+#pragma unroll
+        for (int b = 0; b < D; b++)
+            old[ii][b] = a0 + ii < D ? __ldcs(ol + (size_t)((a0 + ii) * D + b) * hw) : 0.0f;
 }
 
 // Persistent: CTA b handles tiles b, b + gridDim.x, ...; tile t = (edge t / tpe,
@@ -494,7 +516,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (!(P.stall && na == 0)) {
                             mbar_arrive_expect_tx(bar(kBarAFull), P.atoms * kTileM * kRowBytes);
                             const int arow =
-                                (int)((long long)ti.si * g.frame_rows + g.row0[0] + ti.p0);
+                                (int)((long long)ti.si * g.frame_rows + P.a_off + g.row0[0] + ti.p0);
                             for (int k = 0; k < P.atoms; k++)
                                 tma_load_2d(sA + k * kTileM * kRowBytes, &maps.a, k * 64, arow,
                                             bar(kBarAFull));
@@ -734,16 +756,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const bool interior_all = __all_sync(
                     0xffffffffu, !pv || (any && bx >= 0 && bx + NW - 1 < Wl && by >= 0 &&
                                          by + NW - 1 < Hl));
+                constexpr int AW = (D + kSubWarps - 1) / kSubWarps;  // 4, 3 at R = 3
+                float* ol = out_e + (size_t)(l * D * D) * hw + p;
+                float old[AW][D];
+                if (P.accum && pv) load_old<R, AW>(ol, sub * AW, hw, old);
                 quarter_sync(quarter);  // all strips of this level are in the windows
                 if (pv) {
-                    constexpr int AW = (D + kSubWarps - 1) / kSubWarps;  // 4, 3 at R = 3
-                    float* ol = out_e + (size_t)(l * D * D) * hw + p;
                     if (interior_all)
                         bilinear_columns<R, AW, false>(win, swz, kx, sub * AW, bx, by, Wl, Hl,
-                                                       true, dx, dy, g.alpha, ol, hw);
+                                                       true, dx, dy, g.alpha, ol, hw, P.accum,
+                                                       P.keep, old);
                     else
                         bilinear_columns<R, AW, true>(win, swz, kx, sub * AW, bx, by, Wl, Hl, any,
-                                                      dx, dy, g.alpha, ol, hw);
+                                                      dx, dy, g.alpha, ol, hw, P.accum, P.keep,
+                                                      old);
                 }
                 quarter_sync(quarter);  // all are done reading before the next level
                 w_c += DC_PROF_NOW() - t2;
@@ -823,7 +849,7 @@ extern "C" int dc_tc_trace_read(long long* host) {
 
 bool dc_tc_supported(const dc_ctx* ctx) {
     const int p = ctx->cfg.precision;
-    return (p == DC_PREC_FP16 || p == DC_PREC_BF16) &&
+    return (p == DC_PREC_FP16 || p == DC_PREC_BF16 || p == DC_PREC_TF32 || p == DC_PREC_FP32X3) &&
            (ctx->cfg.channels == 64 || ctx->cfg.channels == 128);
 }
 
@@ -850,16 +876,20 @@ int dc_tc_prepare(dc_ctx* ctx) {
                       CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r1 != CUDA_SUCCESS) return dc_fail(ctx, DC_ERR_CUDA, "cuTensorMapEncodeTiled failed");
-    for (int l = 0; l < ctx->cfg.levels; l++) {
-        const LevelBox lb = level_box(ctx, l);
-        cuuint64_t d4[4] = {(cuuint64_t)ctx->cfg.channels, (cuuint64_t)ctx->W[l],
-                            (cuuint64_t)ctx->H[l], (cuuint64_t)ctx->cfg.max_frames};
-        cuuint64_t s4[3] = {(cuuint64_t)row_bytes, (cuuint64_t)ctx->W[l] * row_bytes,
+    for (int l = 0; l < ctx->cfg.levels * (ctx->lo_rows > 0 ? 2 : 1); l++) {
+        const bool lo = l >= ctx->cfg.levels;  // FP32X3: maps of the lo copy
+        const int lv = lo ? l - ctx->cfg.levels : l;
+        const LevelBox lb = level_box(ctx, lv);
+        cuuint64_t d4[4] = {(cuuint64_t)ctx->cfg.channels, (cuuint64_t)ctx->W[lv],
+                            (cuuint64_t)ctx->H[lv], (cuuint64_t)ctx->cfg.max_frames};
+        cuuint64_t s4[3] = {(cuuint64_t)row_bytes, (cuuint64_t)ctx->W[lv] * row_bytes,
                             (cuuint64_t)ctx->frame_rows * row_bytes};
         cuuint32_t b4[4] = {64, (cuuint32_t)lb.wbox, (cuuint32_t)lb.br, 1};
         cuuint32_t e4[4] = {1, 1, 1, 1};
-        void* base = static_cast<char*>(ctx->store) + ctx->level_row0[l] * row_bytes;
-        CUresult r = enc(reinterpret_cast<CUtensorMap*>(ctx->tmap_b[l]), dt, 4, base, d4, s4, b4,
+        void* base = static_cast<char*>(ctx->store) +
+                     (ctx->level_row0[lv] + (lo ? ctx->lo_rows : 0)) * row_bytes;
+        unsigned char* tm = lo ? ctx->tmap_b_lo[lv] : ctx->tmap_b[lv];
+        CUresult r = enc(reinterpret_cast<CUtensorMap*>(tm), dt, 4, base, d4, s4, b4,
                          e4, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (r != CUDA_SUCCESS)
@@ -895,22 +925,33 @@ int dc_launch_tc(dc_ctx* ctx, const int* ii, const int* jj, int M, const float* 
     const int ntiles = (ctx->hw + kTileM - 1) / kTileM * M;
     const int ctas = ctx->max_ctas > 0 && ctx->max_ctas < ctx->num_sms ? ctx->max_ctas : ctx->num_sms;
     dim3 grid(ntiles < ctas ? ntiles : ctas);
-    TcMaps maps;
-    memset(&maps, 0, sizeof(maps));
-    memcpy(&maps.a, ctx->tmap_a, sizeof(CUtensorMap));
-    for (int l = 0; l < ctx->cfg.levels; l++) memcpy(&maps.b[l], ctx->tmap_b[l], sizeof(CUtensorMap));
+    // FP32X3: three passes, hi.hi + hi.lo + lo.hi, the later two adding to `out`
+    const int passes = ctx->lo_rows > 0 ? 3 : 1;
+    for (int pass = 0; pass < passes; pass++) {
+        const bool a_lo = pass == 2, b_lo = pass == 1;
+        P.a_off = a_lo ? ctx->lo_rows : 0;
+        P.accum = pass > 0;
+        P.keep = pass + 1 < passes;
+        TcMaps maps;
+        memset(&maps, 0, sizeof(maps));
+        memcpy(&maps.a, ctx->tmap_a, sizeof(CUtensorMap));
+        for (int l = 0; l < ctx->cfg.levels; l++)
+            memcpy(&maps.b[l], b_lo ? ctx->tmap_b_lo[l] : ctx->tmap_b[l], sizeof(CUtensorMap));
 #define DC_TC_LAUNCH(RR)                                                                 \
     do {                                                                                 \
         auto k = corr_tc_kernel<RR>;                                                     \
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
         k<<<grid, kThreads, smem, s>>>(maps, P);                                         \
     } while (0)
-    switch (ctx->cfg.radius) {
-        case 0: DC_TC_LAUNCH(0); break;
-        case 1: DC_TC_LAUNCH(1); break;
-        case 2: DC_TC_LAUNCH(2); break;
-        default: DC_TC_LAUNCH(3); break;
-    }
+        switch (ctx->cfg.radius) {
+            case 0: DC_TC_LAUNCH(0); break;
+            case 1: DC_TC_LAUNCH(1); break;
+            case 2: DC_TC_LAUNCH(2); break;
+            default: DC_TC_LAUNCH(3); break;
+        }
 #undef DC_TC_LAUNCH
-    return dc_check_launch(ctx, "corr_tc_kernel");
+        const int rc = dc_check_launch(ctx, "corr_tc_kernel");
+        if (rc) return rc;
+    }
+    return DC_OK;
 }

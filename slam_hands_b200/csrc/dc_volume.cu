@@ -230,6 +230,7 @@ int dc_launch_volume_ffma(dc_ctx* ctx, const int* ii, const int* jj, int M, floa
     dim3 grid((g.hw + BT - 1) / BT, (g.hw + BT - 1) / BT, M);
     switch (ctx->cfg.precision) {
         case DC_PREC_FP16:
+        case DC_PREC_TF32:
             volume_ffma_kernel<__half><<<grid, 256, 0, s>>>((const __half*)ctx->store, ii, jj,
                                                             ctx->cfg.max_frames, g, vol0);
             break;
