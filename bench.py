@@ -246,21 +246,13 @@ def main():
     dev = torch.device("cuda", local)
     pg = None
     store = None
-    slot_pg = None
     if world > 1:
         import torch.distributed as dist
 
         dist.init_process_group("nccl", device_id=dev)
         pg = dist
         store = dist.distributed_c10d._get_default_store()
-        # the per-step slot broadcasts get their own communicator capped at 4
-        # CTAs, so that they fit on the 4 SMs the fused kernel leaves free and
-        # run beside it (an uncapped broadcast spreads over more channels than
-        # there are free SMs and finishes only after the kernel)
-        slot_opts = dist.ProcessGroupNCCL.Options()
-        slot_opts.config.max_ctas = 4
-        slot_opts.config.min_ctas = 1
-        slot_pg = dist.new_group(backend="nccl", pg_options=slot_opts)
+
 
     # inputs: frames from rank 0 (seeded, replicated by NCCL broadcast).  The
     # frontend workloads (<= 48 edges, C1/C2/C4 up to 96) give every rank its own
@@ -345,7 +337,7 @@ def main():
             if rank == 0:
                 dc.set_frames(src, first_slot=slot, stream=strm)
             if pg is not None:
-                replicate_store(dc, slot, 1, group=slot_pg)  # stream-ordered; NCCL watchdog bounds it
+                replicate_store(dc, slot, 1)  # stream-ordered; NCCL watchdog bounds it
 
     vols = ([torch.empty(sh, dtype=torch.float32, device=dev) for sh in dc.volume_shapes(M)]
             if args.materialise else None)
