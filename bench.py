@@ -275,8 +275,6 @@ def main():
     # while the current step's kernel reads the others
     dc = DroidCorrelation(wl.h, wl.w, channels=wl.channels, precision=args.precision,
                           alpha=wl.alpha, max_frames=wl.frames + 1, max_edges=M, device=dev)
-    if pg is not None:
-        dc.set_max_ctas(torch.cuda.get_device_properties(dev).multi_processor_count - 4)
     out = torch.empty(M, dc.out_channels, wl.h, wl.w, device=dev)
     # L2 flush between steps: READ a buffer twice the L2 size, so the cache is
     # left holding clean lines (a write flush would leave ~126 MB of dirty lines
