@@ -8,14 +8,16 @@
 // write 128 fp32 channels holding fp16-rounded values.  Here the result is
 // written as fp16 (the same values, half the bytes).
 //
-// Per tile of 128 pixels of one edge (persistent CTAs, 128 threads): thread p
-// reads pixel p's 196 features (coalesced along pixels), rounds them to fp16
-// and writes them to shared memory as the K-major A operand (128-byte swizzle,
-// K padded with zeros to 256); the weights, packed once by dc_set_corr_encoder
+// Per tile of 128 pixels of one edge (persistent CTAs, 512 threads): four
+// threads per pixel each read a quarter of its 196 features (coalesced along
+// pixels, 64 loads in flight per thread), round them to fp16 and write them to
+// shared memory as the K-major A operand (128-byte swizzle, K padded with
+// zeros to 256); the weights, packed once by dc_set_corr_encoder
 // into the same layout, stay resident in shared memory as the B operand; one
 // thread issues 16 tcgen05.mma (kind::f16, M = N = 128, K = 16) into a TMEM
-// accumulator; each warp reads its 32 pixels' 128 outputs back (tcgen05.ld),
-// adds the bias, applies the ReLU, rounds to fp16 and stores 64-byte rows.
+// accumulator; each warp reads 32 outputs of its lane quarter's 32 pixels back
+// (tcgen05.ld), adds the bias, applies the ReLU, rounds to fp16 and stores
+// 64-byte rows.
 // The wait for the MMAs is bounded (2 s) and reports through the context's
 // device error word.
 #include <cuda_fp16.h>
@@ -30,7 +32,8 @@ using namespace dc::sm100;
 constexpr int kEncM = 128;        // pixels per tile (MMA M, TMEM lanes)
 constexpr int kEncCo = 128;       // output channels (MMA N)
 constexpr int kEncK = 256;        // input channels, padded (four 64-element K atoms)
-constexpr int kEncThreads = 128;
+constexpr int kEncThreads = 512;  // 4 threads per pixel row of the tile
+constexpr int kEncParts = kEncThreads / kEncM;
 constexpr uint32_t kAtomBytes = 128u * 128u;            // 128 rows x 128 bytes
 constexpr uint32_t kOperandBytes = 4u * kAtomBytes;     // 64 KB
 constexpr uint32_t kWeightBytes = kOperandBytes;
@@ -96,12 +99,15 @@ __global__ void __launch_bounds__(kEncThreads, 1) corr_encoder_kernel(EncParams 
 
     for (int t = blockIdx.x; t < ntiles && alive; t += gridDim.x, phase ^= 1) {
         const int e = t / tpe, p0 = (t - e * tpe) * kEncM;
-        const int p = p0 + tid;
+        const int row = tid % kEncM, part = tid / kEncM;
+        const int p = p0 + row;
         const bool pv = p < hw;
-        // A tile: row tid = pixel p, 8 channels per 16-byte chunk
+        // A tile: row = pixel p, 8 channels per 16-byte chunk; this thread's
+        // quarter of the chunks, all loads issued before any is used
         const float* src = P.corr + (size_t)e * P.ci * hw + p;
-#pragma unroll 2
-        for (int c = 0; c < kEncK / 8; c++) {
+#pragma unroll
+        for (int cc = 0; cc < kEncK / 8 / kEncParts; cc++) {
+            const int c = part * (kEncK / 8 / kEncParts) + cc;
             float v[8];
 #pragma unroll
             for (int j = 0; j < 8; j++) {
@@ -115,7 +121,7 @@ __global__ void __launch_bounds__(kEncThreads, 1) corr_encoder_kernel(EncParams 
             pk.y = *reinterpret_cast<uint32_t*>(&h1);
             pk.z = *reinterpret_cast<uint32_t*>(&h2);
             pk.w = *reinterpret_cast<uint32_t*>(&h3);
-            *reinterpret_cast<uint4*>(sA + sw128_offset(tid, 8 * c)) = pk;
+            *reinterpret_cast<uint4*>(sA + sw128_offset(row, 8 * c)) = pk;
         }
         fence_proxy_async();  // generic-proxy stores -> tensor-core reads
         tc_fence_before();
@@ -141,20 +147,21 @@ __global__ void __launch_bounds__(kEncThreads, 1) corr_encoder_kernel(EncParams 
         }
         // every warp must reach the barrier below, whether or not it gave up
         if (alive) {
+            // warp w: TMEM lane quarter w % 4 (pixels 32 (w % 4) ..), output
+            // channels 32 (w / 4) .. 32 (w / 4) + 31
             tc_fence_after();
-            const uint32_t tl = tmem + ((uint32_t)(32 * warp) << 16);
-            __half* o = P.out + (size_t)e * kEncCo * hw + p;
+            const int q = warp & 3, cb = 32 * (warp >> 2);
+            const int pq = p0 + 32 * q + lane;
+            const uint32_t tl = tmem + ((uint32_t)(32 * q) << 16) + cb;
+            float acc[32];
+            tmem_ld32(tl, acc);
+            if (pq < hw) {
+                __half* o = P.out + (size_t)e * kEncCo * hw + pq;
 #pragma unroll
-            for (int blk = 0; blk < kEncCo / 64; blk++) {
-                float acc[64];
-                tmem_ld64(tl + 64 * blk, acc);
-                if (pv) {
-#pragma unroll
-                    for (int j = 0; j < 64; j++) {
-                        const int co = 64 * blk + j;
-                        const float y = fmaxf(acc[j] + __ldg(P.bias + co), 0.0f);
-                        o[(size_t)co * hw] = __float2half_rn(y);
-                    }
+                for (int j = 0; j < 32; j++) {
+                    const int co = cb + j;
+                    const float y = fmaxf(acc[j] + __ldg(P.bias + co), 0.0f);
+                    o[(size_t)co * hw] = __float2half_rn(y);
                 }
             }
         }
