@@ -359,3 +359,16 @@ def test_store_slots_copy_equals_local_pack(cuda):
     assert torch.equal(a, b)
     with pytest.raises(DroidCorrError):
         dc.store_slots(2, 3)
+
+
+def test_cta_cap_does_not_change_results(cuda):
+    # dc_set_max_ctas (CTAs of the persistent fused kernel) changes the tile
+    # schedule only, never a result bit
+    h, w = 48, 64
+    dc, fm, ii, jj, coords = setup(h, w, K=4, precision="fp16", M=6, sigma=3.0)
+    c = torch.from_numpy(coords).cuda()
+    full = dc.build_and_lookup(ii, jj, c)
+    for cap in (1, 7, 144):
+        dc.set_max_ctas(cap)
+        assert torch.equal(dc.build_and_lookup(ii, jj, c), full)
+    dc.set_max_ctas(0)
