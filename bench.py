@@ -271,10 +271,12 @@ def main():
         g.manual_seed(configs.SEED + 7 * rank)
         base = torch.from_numpy(configs.grid_coords(wl.h, wl.w)).to(dev)[None]
         coords = (base + torch.randn(M, 2, wl.h, wl.w, generator=g, device=dev) * wl.sigma).contiguous()
-    # one spare slot: the next step's keyframe is packed (and broadcast) into it
-    # while the current step's kernel reads the others
+    # two spare slots: the keyframe of step k + 2 is packed (and replicated)
+    # while step k's kernel reads the others, so the transfer between GPUs has
+    # a whole step of slack
+    SPARES = 2
     dc = DroidCorrelation(wl.h, wl.w, channels=wl.channels, precision=args.precision,
-                          alpha=wl.alpha, max_frames=wl.frames + 1, max_edges=M, device=dev)
+                          alpha=wl.alpha, max_frames=wl.frames + SPARES, max_edges=M, device=dev)
     out = torch.empty(M, dc.out_channels, wl.h, wl.w, device=dev)
     # L2 flush between steps: READ a buffer twice the L2 size, so the cache is
     # left holding clean lines (a write flush would leave ~126 MB of dirty lines
@@ -287,7 +289,6 @@ def main():
 
     # ---- the resident keyframe graph: rank 0 packs every keyframe once and one
     # NCCL broadcast of the packed store reaches the other ranks (timed apart)
-    ring = SlotRing(wl.frames)
     if rank == 0:
         dc.set_frames(fm)
     torch.cuda.synchronize()
@@ -310,12 +311,27 @@ def main():
                                "from rank 0, once, before the timed steps",
                        "bytes": nbytes, "ms": rms, "GBs": nbytes / (rms * 1e-3) / 1e9}
 
+    # ---- per-step keyframes on several GPUs: the other ranks pull rank 0's new
+    # packed slot through the copy engines over NVLink (CUDA IPC: rank 0's store
+    # opened in every process), so no SM is spent on the transfer and it
+    # overlaps the fused kernel.  Stream-ordered counters in rank 0's store page
+    # order pack -> pull (word 0 = last packed step + 1) and pull -> the next
+    # pack (word r = rank r's last pulled step + 1), with no host round trip.
+    ipc = False
+    if pg is not None and frontend:
+        if rank == 0:
+            store.set("dc/ipc/store", dc.store_ipc_handle())
+        else:
+            dc.attach_source(store.get("dc/ipc/store"))
+        pg.barrier()
+        ipc = True
+
     # ---- per step (frontend workloads): keyframe f = k % frames arrives; rank 0
     # packs it into the ring's spare slot and broadcasts that slot, while the
     # step's kernel runs on the previous mapping; edges are translated to slots
     n_steps_all = max(args.warmup, 3) + args.steps + 2 * (3 + args.steps) + 2
     step_edges = []
-    ring_sim = SlotRing(wl.frames)
+    ring_sim = SlotRing(wl.frames, spares=SPARES)
     for k in range(n_steps_all):
         f = k % wl.frames
         slot = ring_sim.begin(f)
@@ -333,8 +349,17 @@ def main():
         src = fm[f:f + 1] if fm_src is None else fm_src
         with torch.cuda.stream(strm):
             if rank == 0:
+                if ipc and k >= 1:
+                    for r in range(1, world):  # every rank has pulled keyframe k - 1
+                        dc.sync_wait(r, k, stream=strm)
                 dc.set_frames(src, first_slot=slot, stream=strm)
-            if pg is not None:
+                if ipc:
+                    dc.sync_signal(0, k + 1, stream=strm)
+            elif ipc:
+                dc.sync_wait(0, k + 1, remote=True, stream=strm)
+                dc.pull_slots(slot, 1, stream=strm)
+                dc.sync_signal(rank, k + 1, remote=True, stream=strm)
+            if pg is not None and not ipc:
                 replicate_store(dc, slot, 1)  # stream-ordered; NCCL watchdog bounds it
 
     vols = ([torch.empty(sh, dtype=torch.float32, device=dev) for sh in dc.volume_shapes(M)]
@@ -376,12 +401,18 @@ def main():
             dc.build_and_lookup(ii_, jj_, coords_, out_)
 
     k_glob = 0  # next step index (into step_edges)
+    prep_done = {}
     if frontend:
-        prep(0, stream)
+        for k0 in range(SPARES):
+            prep(k0, stream)
+            prep_done[k0] = torch.cuda.Event()
+            prep_done[k0].record(stream)
 
     def step(record_ev=None):
         """Step k: kernel k on the current slots beside the keyframe of step
-        k + 1 (packed + broadcast on a side stream); both end inside the step."""
+        k + 2 (packed and replicated on a side stream); the step ends when the
+        kernel and the keyframe of step k + 1 (prepared during step k - 1) are
+        both in place."""
         nonlocal k_glob
         k = k_glob
         if record_ev is not None:
@@ -390,16 +421,16 @@ def main():
             ev_go = torch.cuda.Event()
             ev_go.record(stream)
             s_rep.wait_event(ev_go)
-            prep(k + 1, s_rep)
-            ev_prep = torch.cuda.Event()
-            ev_prep.record(s_rep)
+            prep(k + SPARES, s_rep)
+            prep_done[k + SPARES] = torch.cuda.Event()
+            prep_done[k + SPARES].record(s_rep)
         if record_ev is not None:
             record_ev[2].record(stream)
         corr(k, record=record_ev is not None)
         if record_ev is not None:
             record_ev[3].record(stream)
         if frontend:
-            stream.wait_event(ev_prep)
+            stream.wait_event(prep_done.pop(k + 1))
         if record_ev is not None:
             record_ev[1].record(stream)
         k_glob += 1
@@ -423,6 +454,13 @@ def main():
     torch.cuda.synchronize()
     launches0 = dc.launch_count
     torch.cuda._sleep(int(0.02 * 1.9e9))
+    if pg is not None:
+        # align the GPUs' timelines after the sleep (a one-float all-reduce on the
+        # launching stream, outside the step events): the ranks' steps are
+        # coupled through the keyframe replication, so a start skew would
+        # otherwise be charged to the first steps of the earlier rank
+        align = torch.zeros(1, device=dev)
+        pg.all_reduce(align)
     for s in range(args.steps):
         torch.sum(flush, dim=0, out=flush_sink)
         step(ev[s])
@@ -654,8 +692,9 @@ def main():
                                   if proj is not None else ""),
                    "alpha": wl.alpha, "l2": "flushed between steps (252 MB read)",
                    "step": ("one keyframe arrives per step: packed into the spare store slot "
-                            "(and NCCL-broadcast to the other ranks) beside the step's kernel "
-                            "over the resident keyframe graph" if frontend else
+                            "(other ranks pull it from rank 0 over NVLink with the copy "
+                            "engines) beside the step's kernel over the resident keyframe "
+                            "graph" if frontend else
                             "one backend pass over the resident keyframe graph (keyframes "
                             "replicated once before the timed steps, see replication)"),
                    "parallelism": f"edges sharded, dp{world}"},

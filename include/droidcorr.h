@@ -137,6 +137,33 @@ int dc_set_frames(dc_ctx* ctx, const void* fmaps_dev, int dtype, int first_slot,
 int dc_store_slots(dc_ctx* ctx, int first_slot, int count, void** ptr_out,
                    long long* bytes_out);
 
+/* Replication of packed keyframes between processes (one per GPU) through the
+ * copy engines over NVLink, no SMs involved: the owner exports its store with
+ * dc_store_ipc_handle (DC_IPC_HANDLE_BYTES bytes, a CUDA IPC memory handle, to
+ * be passed to the other processes by the host); each other process attaches
+ * it once with dc_store_attach_source -- both contexts must have been created
+ * with the same dc_config -- and copies slots with dc_store_pull_slots, an
+ * asynchronous device-to-device copy on `stream`.  The caller orders the pull
+ * after the owner's dc_set_frames of those slots (e.g. an interprocess CUDA
+ * event) and keeps the owner from rewriting slots being pulled.  No reference
+ * counterpart: the reference runs on one GPU. */
+#define DC_IPC_HANDLE_BYTES 64
+int dc_store_ipc_handle(dc_ctx* ctx, void* handle_out);
+int dc_store_attach_source(dc_ctx* ctx, const void* handle);
+int dc_store_pull_slots(dc_ctx* ctx, int first_slot, int count, dc_stream_t stream);
+
+/* Stream-ordered counters for that replication, with no host round trip and
+ * no SM: every store carries a page of 1024 32-bit words (zero at creation).
+ * dc_sync_signal writes `value` to word `word` of this context's page
+ * (remote = 0) or of the attached source's page over NVLink (remote = 1) once
+ * the stream's earlier work is done; dc_sync_wait holds the stream until that
+ * word is >= value (cuStreamWriteValue32 / cuStreamWaitValue32).  Counters are
+ * meant to grow (e.g. the step index + 1).  A wait whose value never comes
+ * holds its stream until the process ends: use them between processes that
+ * run the same step sequence, with host-side liveness checks between steps. */
+int dc_sync_signal(dc_ctx* ctx, int word, unsigned value, int remote, dc_stream_t stream);
+int dc_sync_wait(dc_ctx* ctx, int word, unsigned value, int remote, dc_stream_t stream);
+
 /* Materialised volumes for M edges (CudaDroid::build_correlation, main.cu:1500,
  * and steps 1-3 of batch_build_and_sample_correlation, main.cu:1558-1596):
  * vol0 = alpha * f_ii^T f_jj, then vol_l = 2x2 average of vol_{l-1} over the

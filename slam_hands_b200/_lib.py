@@ -73,6 +73,11 @@ SIGNATURES = {
                                         _vp, _vp, _vp]),
     "dc_static_device_status": (_i, [_vp]),
     "dc_set_max_ctas": (_i, [_vp, _i]),
+    "dc_store_ipc_handle": (_i, [_vp, _vp]),
+    "dc_store_attach_source": (_i, [_vp, _vp]),
+    "dc_store_pull_slots": (_i, [_vp, _i, _i, _vp]),
+    "dc_sync_signal": (_i, [_vp, _i, ctypes.c_uint, _i, _vp]),
+    "dc_sync_wait": (_i, [_vp, _i, ctypes.c_uint, _i, _vp]),
     "dc_set_corr_encoder": (_i, [_vp, _vp, _vp, _i, _vp]),
     "dc_corr_encode": (_i, [_vp, _vp, _i, _vp, _vp]),
     "dc_build_lookup_encode": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp, _vp]),

@@ -125,6 +125,33 @@ class DroidCorrelation:
         self._check(self.lib.dc_set_frames(self._ctx, fmaps.data_ptr(), dt, first_slot,
                                            fmaps.shape[0], _stream(stream)))
 
+    def store_ipc_handle(self) -> bytes:
+        """CUDA IPC handle of the packed store, for dc_store_attach_source in
+        another process (dc_store_ipc_handle)."""
+        buf = ctypes.create_string_buffer(64)
+        self._check(self.lib.dc_store_ipc_handle(self._ctx, buf))
+        return buf.raw
+
+    def attach_source(self, handle: bytes) -> None:
+        """Open another process's store (same configuration) as the source of
+        pull_slots (dc_store_attach_source)."""
+        self._check(self.lib.dc_store_attach_source(self._ctx, ctypes.c_char_p(bytes(handle))))
+
+    def pull_slots(self, first_slot: int, count: int,
+                   stream: Optional[torch.cuda.Stream] = None) -> None:
+        """Copy store slots from the attached source store (copy engine, async)."""
+        self._check(self.lib.dc_store_pull_slots(self._ctx, first_slot, count, _stream(stream)))
+
+    def sync_signal(self, word: int, value: int, remote: bool = False,
+                    stream: Optional[torch.cuda.Stream] = None) -> None:
+        """Stream-ordered write of a replication counter (dc_sync_signal)."""
+        self._check(self.lib.dc_sync_signal(self._ctx, word, value, int(remote), _stream(stream)))
+
+    def sync_wait(self, word: int, value: int, remote: bool = False,
+                  stream: Optional[torch.cuda.Stream] = None) -> None:
+        """Hold the stream until a replication counter reaches value (dc_sync_wait)."""
+        self._check(self.lib.dc_sync_wait(self._ctx, word, value, int(remote), _stream(stream)))
+
     def store_slots(self, first_slot: int, count: int) -> torch.Tensor:
         """uint8 view [bytes] of the packed store slots first_slot..+count (device
         memory owned by the library; valid while this object lives)."""

@@ -4,6 +4,8 @@
 #include <cstdio>
 #include <cstring>
 
+#include <cuda.h>
+
 #include "dc_internal.cuh"
 
 int dc_fail(dc_ctx* ctx, int status, const std::string& msg) {
@@ -20,6 +22,26 @@ int dc_check_launch(dc_ctx* ctx, const char* what) {
 }
 
 namespace {
+
+constexpr long long kSyncPageBytes = 4096;
+constexpr int kSyncWords = (int)(kSyncPageBytes / 4);
+
+typedef CUresult (*StreamValueFn)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
+
+StreamValueFn stream_value_fn(const char* name) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+        return nullptr;
+    return reinterpret_cast<StreamValueFn>(p);
+}
+
+// Word `word` of this context's counter page, or of the attached source's.
+CUdeviceptr sync_word(const dc_ctx* ctx, int word, bool remote) {
+    const char* base = static_cast<const char*>(remote ? ctx->src_store : ctx->store);
+    return reinterpret_cast<CUdeviceptr>(base + ctx->store_bytes + 4LL * word);
+}
 
 int validate_edges(dc_ctx* ctx, const int* ii, const int* jj, int M) {
     if (M < 0 || M > ctx->cfg.max_edges)
@@ -104,13 +126,14 @@ int dc_create(const dc_config* cfg, dc_ctx** out) {
         return DC_ERR_CUDA;
     }
     cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, ctx->device);
-    if (cudaMalloc(&ctx->store, ctx->store_bytes) != cudaSuccess) {
+    // the store, then one 4 KB page of replication counters (dc_sync_signal)
+    if (cudaMalloc(&ctx->store, ctx->store_bytes + kSyncPageBytes) != cudaSuccess) {
         cudaGetLastError();
         delete ctx;
         return DC_ERR_NO_MEMORY;
     }
     // Padding rows must read as zero; the store is written slot by slot later.
-    if (cudaMemset(ctx->store, 0, ctx->store_bytes) != cudaSuccess ||
+    if (cudaMemset(ctx->store, 0, ctx->store_bytes + kSyncPageBytes) != cudaSuccess ||
         cudaDeviceSynchronize() != cudaSuccess) {
         cudaFree(ctx->store);
         delete ctx;
@@ -147,6 +170,7 @@ int dc_destroy(dc_ctx* ctx) {
     if (ctx->store) cudaFree(ctx->store);
     if (ctx->dev_err) cudaFree(ctx->dev_err);
     if (ctx->enc_w) cudaFree(ctx->enc_w);
+    if (ctx->src_store) cudaIpcCloseMemHandle(ctx->src_store);
     if (prev >= 0) cudaSetDevice(prev);
     delete ctx;
     return DC_OK;
@@ -184,6 +208,70 @@ int dc_store_slots(dc_ctx* ctx, int first, int count, void** ptr, long long* byt
     const long long slot_bytes = ctx->frame_rows * ctx->cfg.channels * ctx->elem_bytes;
     *ptr = static_cast<char*>(ctx->store) + first * slot_bytes;
     *bytes = count * slot_bytes;
+    return DC_OK;
+}
+
+int dc_store_ipc_handle(dc_ctx* ctx, void* handle_out) {
+    if (!ctx || !handle_out) return DC_ERR_INVALID_ARG;
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, ctx->store) != cudaSuccess) {
+        cudaGetLastError();
+        return dc_fail(ctx, DC_ERR_CUDA, "cudaIpcGetMemHandle of the store failed");
+    }
+    static_assert(sizeof(h) == DC_IPC_HANDLE_BYTES, "IPC handle size");
+    std::memcpy(handle_out, &h, sizeof(h));
+    return DC_OK;
+}
+
+int dc_store_attach_source(dc_ctx* ctx, const void* handle) {
+    if (!ctx || !handle) return DC_ERR_INVALID_ARG;
+    if (ctx->src_store) return dc_fail(ctx, DC_ERR_INVALID_ARG, "a source store is attached");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    void* p = nullptr;
+    if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        cudaGetLastError();
+        return dc_fail(ctx, DC_ERR_CUDA, "cudaIpcOpenMemHandle of the source store failed");
+    }
+    ctx->src_store = p;
+    return DC_OK;
+}
+
+int dc_store_pull_slots(dc_ctx* ctx, int first, int count, dc_stream_t stream) {
+    if (!ctx) return DC_ERR_INVALID_ARG;
+    if (!ctx->src_store) return dc_fail(ctx, DC_ERR_NOT_READY, "no source store attached");
+    if (first < 0 || count < 0 || first + count > ctx->cfg.max_frames)
+        return dc_fail(ctx, DC_ERR_INVALID_ARG, "slot range outside [0, max_frames)");
+    if (count == 0) return DC_OK;
+    const long long slot_bytes = ctx->frame_rows * ctx->cfg.channels * ctx->elem_bytes;
+    if (cudaMemcpyAsync(static_cast<char*>(ctx->store) + first * slot_bytes,
+                        static_cast<const char*>(ctx->src_store) + first * slot_bytes,
+                        (size_t)(count * slot_bytes), cudaMemcpyDeviceToDevice,
+                        (cudaStream_t)stream) != cudaSuccess) {
+        cudaGetLastError();
+        return dc_fail(ctx, DC_ERR_CUDA, "copying slots from the source store failed");
+    }
+    return DC_OK;
+}
+
+int dc_sync_signal(dc_ctx* ctx, int word, unsigned value, int remote, dc_stream_t stream) {
+    if (!ctx || word < 0 || word >= kSyncWords) return DC_ERR_INVALID_ARG;
+    if (remote && !ctx->src_store) return dc_fail(ctx, DC_ERR_NOT_READY, "no source store attached");
+    static StreamValueFn fn = stream_value_fn("cuStreamWriteValue32");
+    if (!fn) return dc_fail(ctx, DC_ERR_UNSUPPORTED, "cuStreamWriteValue32 unavailable");
+    if (fn((CUstream)stream, sync_word(ctx, word, remote != 0), value, 0) != CUDA_SUCCESS)
+        return dc_fail(ctx, DC_ERR_CUDA, "cuStreamWriteValue32 failed");
+    return DC_OK;
+}
+
+int dc_sync_wait(dc_ctx* ctx, int word, unsigned value, int remote, dc_stream_t stream) {
+    if (!ctx || word < 0 || word >= kSyncWords) return DC_ERR_INVALID_ARG;
+    if (remote && !ctx->src_store) return dc_fail(ctx, DC_ERR_NOT_READY, "no source store attached");
+    static StreamValueFn fn = stream_value_fn("cuStreamWaitValue32");
+    if (!fn) return dc_fail(ctx, DC_ERR_UNSUPPORTED, "cuStreamWaitValue32 unavailable");
+    // CU_STREAM_WAIT_VALUE_GEQ: counters only grow
+    if (fn((CUstream)stream, sync_word(ctx, word, remote != 0), value, 0x0) != CUDA_SUCCESS)
+        return dc_fail(ctx, DC_ERR_CUDA, "cuStreamWaitValue32 failed");
     return DC_OK;
 }
 

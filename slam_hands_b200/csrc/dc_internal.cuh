@@ -32,6 +32,7 @@ struct dc_ctx {
     long long lo_rows = 0;  // DC_PREC_FP32X3: a slot holds hi rows, then the lo copy at +lo_rows
     int elem_bytes = 4;
     void* store = nullptr;  // device
+    void* src_store = nullptr;  // another process's store, opened by dc_store_attach_source
     long long store_bytes = 0;
     int num_sms = 148;
     int max_ctas = 0;  // cap on the CTAs of the persistent fused kernel (0: one per SM)

@@ -83,26 +83,35 @@ def replicate_store(dc, first_slot: int, count: int, src: int = 0, group=None,
 
 
 class SlotRing:
-    """Keyframe slots of the packed store with one spare slot, so that a new
-    keyframe can be packed (and broadcast) while kernels of the previous step
+    """Keyframe slots of the packed store with spare slots, so that the next
+    keyframes can be packed (and replicated) while kernels of earlier steps
     still read the old ones.
 
-    The store holds `frames + 1` slots.  Logical keyframe f lives in physical
-    slot `phys[f]`; `spare` is unused.  `begin(f)` names the slot that receives
-    f's new feature map (the spare); `commit(f)` makes it f's slot and the old
-    one the spare.  Edge lists are given in logical ids and translated with
-    `slots(ii)`.  (The reference stores keyframe k in DroidState::fmaps[k],
-    cuda_slam/main.cu:755, synchronously, on one GPU.)"""
+    The store holds `frames + spares` slots.  Logical keyframe f lives in
+    physical slot `phys[f]`; the spare slots wait in a FIFO.  `begin(f)` names
+    the slot that receives f's new feature map (the oldest spare); `commit(f)`
+    makes it f's slot and queues f's old slot as a spare.  A slot handed out by
+    begin() at step j was last read by kernels of step j - spares - 1, so the
+    keyframe of step j may be prepared during step j - spares + 1.  Edge lists
+    are given in logical ids and translated with `slots(ii)`.  (The reference
+    stores keyframe k in DroidState::fmaps[k], cuda_slam/main.cu:755,
+    synchronously, on one GPU.)"""
 
-    def __init__(self, frames: int):
+    def __init__(self, frames: int, spares: int = 1):
         self.phys = list(range(frames))
-        self.spare = frames
+        self.spares = list(range(frames, frames + spares))
+
+    @property
+    def spare(self) -> int:
+        return self.spares[0]
 
     def begin(self, f: int) -> int:
-        return self.spare
+        return self.spares[0]
 
     def commit(self, f: int) -> None:
-        self.phys[f], self.spare = self.spare, self.phys[f]
+        new = self.spares.pop(0)
+        self.spares.append(self.phys[f])
+        self.phys[f] = new
 
     def slots(self, ids):
         return [self.phys[int(i)] for i in ids]

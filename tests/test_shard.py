@@ -131,3 +131,17 @@ def test_slot_ring_keeps_a_spare_slot():
         ring.commit(f)
         assert ring.phys[f] == new and ring.spare == old
         assert sorted(ring.phys + [ring.spare]) == list(range(5))  # a permutation of the slots
+
+
+def test_slot_ring_with_two_spares_reuses_a_slot_three_steps_later():
+    from slam_hands_b200.shard import SlotRing
+    ring = SlotRing(3, spares=2)
+    written = []
+    for k in range(12):
+        f = k % 3
+        written.append(ring.begin(f))
+        ring.commit(f)
+        assert sorted(ring.phys + ring.spares) == list(range(5))
+    # a slot handed out at step j held keyframe data read up to step j - 3
+    for j in range(3, 12):
+        assert written[j] not in written[j - 2:j]
