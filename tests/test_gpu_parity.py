@@ -372,3 +372,21 @@ def test_cta_cap_does_not_change_results(cuda):
         dc.set_max_ctas(cap)
         assert torch.equal(dc.build_and_lookup(ii, jj, c), full)
     dc.set_max_ctas(0)
+
+
+@pytest.mark.parametrize("precision", ["fp16", "bf16", "fp32x3", "tf32"])
+@pytest.mark.parametrize("radius,levels,C", [(0, 1, 128), (1, 2, 64), (2, 3, 128), (3, 4, 64)])
+def test_fused_other_radii_levels_channels(cuda, oracle, precision, radius, levels, C):
+    # the fused tensor-core kernel at every radius template, pyramid depth and
+    # K-atom count it supports, against the fp64 oracle
+    h, w = 40, 72
+    alpha = 1 / math.sqrt(C)
+    dc, fm, ii, jj, coords = setup(h, w, K=3, C=C, precision=precision, M=3, sigma=4.0,
+                                   alpha=alpha, levels=levels, radius=radius)
+    out = dc.build_and_lookup(ii, jj, torch.from_numpy(coords).cuda()).cpu().numpy()
+    assert dc.lib.dc_device_status(dc._ctx, None) == 0
+    assert out.shape == (3, levels * (2 * radius + 1) ** 2, h, w)
+    exp = oracle_alt(oracle, fm, ii, jj, coords, alpha, precision, levels=levels, radius=radius)
+    err = normwise(out, exp)
+    print(f"r={radius} L={levels} C={C} {precision}: normwise {err:.3e}")
+    assert err < (TOL_FP32 if precision == "fp32x3" else 1e-4)
