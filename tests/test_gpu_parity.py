@@ -153,7 +153,8 @@ def test_build_volume_low_precision(cuda, oracle, precision):
 
 @pytest.mark.parametrize("precision", ["fp32", "fp16", "bf16", "tf32", "fp32x3"])
 @pytest.mark.parametrize("entry", ["build_and_lookup", "alt_lookup"])
-@pytest.mark.parametrize("h,w,sigma", [(48, 64, 4.0), (41, 73, 8.0), (54, 96, 3.0), (12, 16, 2.0), (20, 36, 5.0)])
+@pytest.mark.parametrize("h,w,sigma", [(48, 64, 4.0), (41, 73, 8.0), (54, 96, 3.0), (12, 16, 2.0),
+                                       (20, 36, 5.0), (10, 300, 6.0)])
 def test_fused_and_alt_vs_oracle(cuda, oracle, precision, entry, h, w, sigma):
     alpha = 1 / math.sqrt(128)
     dc, fm, ii, jj, coords = setup(h, w, precision=precision, M=2, sigma=sigma, alpha=alpha)
