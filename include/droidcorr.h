@@ -23,6 +23,9 @@
  *                                     main.cu:2188-2201
  *   GraphAgg scatter_mean loop        main.cu:2255-2294    dc_scatter_mean
  *   per-edge inps[ii[e]] copy loop    main.cu:2215-2224    dc_gather_rows
+ *   corr_enc_0 + relu + round_to_fp16 main.cu:552-553,      dc_set_corr_encoder,
+ *   (UpdateModule::forward)           :603-606              dc_corr_encode,
+ *                                                           dc_build_lookup_encode
  *   cuda_pipeline/slam.cuh:2796, :2825, :2851              the same three entry points
  *
  * Conventions (all entry points):
