@@ -23,9 +23,9 @@
 //      touches only strips bx/8 and bx/8 + 1 of each of its rows (a 32-bit mask
 //      over the chunk's strips), so a lane copies a strip it needs into slot 0
 //      or 1 of its window row with two 16-byte stores -- no per-tap selection;
-//   5. after the last chunk of a level, forms the (2r+1)^2 bilinear outputs in
-//      the reference's order of accumulation (main.cu:1196-1213), reading window
-//      column x at slot column (bx mod 8) + x, and stores them as
+//   5. after the last chunk of a level, forms the (2r+1)^2 bilinear outputs
+//      with the reference's weights (main.cu:1196-1213), evaluated separably,
+//      reading window column x at slot column (bx mod 8) + x, and stores them as
 //      out[e][l*(2r+1)^2 + a*(2r+1) + b][p] (consecutive pixels per warp).
 //
 // Warp roles (320 threads): warp 0 schedules tiles and issues TMA, warp 1
@@ -239,15 +239,16 @@ __device__ __forceinline__ void quarter_sync(int quarter) {
 }
 
 // Bilinear outputs of one pixel and level for output columns a0 .. a0 + AW - 1
-// (the window columns are x offsets a, the rows y offsets b), in the
-// reference's order of accumulation (batch_corr_sample_kernel,
-// main.cu:1196-1213): taps (a,b), (a,b+1), (a+1,b), (a+1,b+1), each as
-// fmaf(tap * wx, wy, acc) from +0.  The window holds raw dot products, so alpha
+// (the window columns are x offsets a, the rows y offsets b): the weights of
+// batch_corr_sample_kernel (main.cu:1196-1213), evaluated separably -- first
+// along x per window row (h_j = tap[a][j] wx0 + tap[a+1][j] wx1), then along y
+// (h_b (1 - dy) + h_{b+1} dy) -- which takes 30 instead of 50 operations per
+// output column; the rounding differs from the reference's four-term chain by
+// a few fp32 ulps, far inside the fused path's tolerance (its dot products
+// are tensor-core sums anyway).  The window holds raw dot products, so alpha
 // rides on the x weights.  kCheck: some taps may lie outside the level; they
-// read as +0, which leaves every fmaf unchanged, as skipping them does in the
-// reference; so do all taps of a pixel with no window in the level (any false).
-// Output column a streams column a times (1 - dx) and column a + 1
-// times dx.
+// read as +0, as skipping them does in the reference; so do all taps of a
+// pixel with no window in the level (any false).
 template <int R, int AW, bool kCheck>
 __device__ __forceinline__ void bilinear_columns(const float* win, int swz, int kx, int a0, int bx,
                                                  int by, int Wl, int Hl, bool any, float dx,
@@ -278,12 +279,13 @@ __device__ __forceinline__ void bilinear_columns(const float* win, int swz, int 
         }
         if (ii > 0 && a0 + ii - 1 < D) {
             float* o = ol + (size_t)((a0 + ii - 1) * D) * hw;
+            // separable: interpolate along x per window row, then along y
+            float hx[NW];
+#pragma unroll
+            for (int j = 0; j < NW; j++) hx[j] = fmaf(tap[j], vx_w, pu[j]);
 #pragma unroll
             for (int b = 0; b < D; b++) {
-                float acc = fmaf(pu[b], uy, 0.0f);
-                acc = fmaf(pu[b + 1], dy, acc);
-                acc = fmaf(tap[b] * vx_w, uy, acc);
-                acc = fmaf(tap[b + 1] * vx_w, dy, acc);
+                float acc = fmaf(hx[b + 1], dy, hx[b] * uy);
                 if (accum) acc = old[ii - 1][b] + acc;  // FP32X3 passes 2, 3 add their products
                 if (keep)
                     *o = acc;  // read again by the next FP32X3 pass: keep it in L2
