@@ -314,7 +314,9 @@ __device__ __forceinline__ void load_old(const float* ol, int a0, int hw,
 
 // Persistent: CTA b handles tiles b, b + gridDim.x, ...; tile t = (edge t / tpe,
 // source pixels 128 * (t % tpe) ..).
-template <int R>
+// kSplit: a pass of DC_PREC_FP32X3 (may add to `out` and keep it in L2); the
+// other precisions run the variant without that code.
+template <int R, bool kSplit>
 __global__ void __launch_bounds__(kThreads, 1)
     corr_tc_kernel(const __grid_constant__ TcMaps maps, TcParams P) {
     constexpr int D = 2 * R + 1, NW = 2 * R + 2;
@@ -758,14 +760,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 constexpr int AW = (D + kSubWarps - 1) / kSubWarps;  // 4, 3 at R = 3
                 float* ol = out_e + (size_t)(l * D * D) * hw + p;
                 float old[AW][D];
-                if (P.accum && pv) load_old<R, AW>(ol, sub * AW, hw, old);
+                const bool accum = kSplit && P.accum, keep = kSplit && P.keep;
+                if (accum && pv) load_old<R, AW>(ol, sub * AW, hw, old);
                 quarter_sync(quarter);  // all strips of this level are in the windows
                 // one (checked) variant only: a second, unchecked copy for
                 // interior windows made the kernel 3 % slower -- the epilogue is
                 // sensitive to its instruction footprint
                 if (pv)
                     bilinear_columns<R, AW, true>(win, swz, kx, sub * AW, bx, by, Wl, Hl, any, dx,
-                                                  dy, g.alpha, ol, hw, P.accum, P.keep, old);
+                                                  dy, g.alpha, ol, hw, accum, keep, old);
                 quarter_sync(quarter);  // all are done reading before the next level
                 w_c += DC_PROF_NOW() - t2;
             }
@@ -934,7 +937,7 @@ int dc_launch_tc(dc_ctx* ctx, const int* ii, const int* jj, int M, const float* 
             memcpy(&maps.b[l], b_lo ? ctx->tmap_b_lo[l] : ctx->tmap_b[l], sizeof(CUtensorMap));
 #define DC_TC_LAUNCH(RR)                                                                 \
     do {                                                                                 \
-        auto k = corr_tc_kernel<RR>;                                                     \
+        auto k = passes > 1 ? corr_tc_kernel<RR, true> : corr_tc_kernel<RR, false>;     \
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
         k<<<grid, kThreads, smem, s>>>(maps, P);                                         \
     } while (0)
