@@ -435,38 +435,32 @@ __global__ void __launch_bounds__(kThreads, 1)
             DC_TC_LOAD_COORDS(t + gridDim.x);
             const int e = t / tpe, p0 = (t - e * tpe) * kTileM;
             const bool valid = si >= 0 && si < P.max_frames && sj >= 0 && sj < P.max_frames;
-            int ylo_[DC_MAX_LEVELS], yhi_[DC_MAX_LEVELS], xlo_[DC_MAX_LEVELS],
-                xhi_[DC_MAX_LEVELS];
-#pragma unroll
+            int n = 0;
+            // one level at a time (a rolled loop: the producer shares its SM
+            // sub-partition's instruction cache with two epilogue warps)
+#pragma unroll 1
             for (int l = 0; l < DC_MAX_LEVELS; l++) {
-                ylo_[l] = xlo_[l] = 0x7fffffff;
-                yhi_[l] = xhi_[l] = -1;
-            }
+                int ylo_ = 0x7fffffff, yhi_ = -1, xlo_ = 0x7fffffff, xhi_ = -1;
+                if (l < g.levels) {
+                    const float sc = 1.0f / (float)(1 << l);
 #pragma unroll
-            for (int k = 0; k < kTileM / 32; k++) {
-                if (!(valid && p0 + lane + 32 * k < hw)) continue;
-#pragma unroll
-                for (int l = 0; l < DC_MAX_LEVELS; l++) {
-                    if (l >= g.levels) break;
-                    const float s = 1.0f / (float)(1 << l);
-                    const int by = (int)floorf(cy[k] * s) - R, bx = (int)floorf(cx[k] * s) - R;
-                    const int a0 = max(by, 0), a1 = min(by + NW - 1, g.H[l] - 1);
-                    const int b0 = max(bx, 0), b1 = min(bx + NW - 1, g.W[l] - 1);
-                    if (a0 <= a1 && b0 <= b1) {
-                        ylo_[l] = min(ylo_[l], a0);
-                        yhi_[l] = max(yhi_[l], a1);
-                        xlo_[l] = min(xlo_[l], b0);
-                        xhi_[l] = max(xhi_[l], b1);
+                    for (int k = 0; k < kTileM / 32; k++) {
+                        if (!(valid && p0 + lane + 32 * k < hw)) continue;
+                        const int by = (int)floorf(cy[k] * sc) - R, bx = (int)floorf(cx[k] * sc) - R;
+                        const int a0 = max(by, 0), a1 = min(by + NW - 1, g.H[l] - 1);
+                        const int b0 = max(bx, 0), b1 = min(bx + NW - 1, g.W[l] - 1);
+                        if (a0 <= a1 && b0 <= b1) {
+                            ylo_ = min(ylo_, a0);
+                            yhi_ = max(yhi_, a1);
+                            xlo_ = min(xlo_, b0);
+                            xhi_ = max(xhi_, b1);
+                        }
                     }
                 }
-            }
-            int n = 0;
-#pragma unroll
-            for (int l = 0; l < DC_MAX_LEVELS; l++) {
-                const int ylo = __reduce_min_sync(0xffffffffu, ylo_[l]);
-                const int yhi = __reduce_max_sync(0xffffffffu, yhi_[l]);
-                const int xlo = __reduce_min_sync(0xffffffffu, xlo_[l]);
-                const int xhi = __reduce_max_sync(0xffffffffu, xhi_[l]);
+                const int ylo = __reduce_min_sync(0xffffffffu, ylo_);
+                const int yhi = __reduce_max_sync(0xffffffffu, yhi_);
+                const int xlo = __reduce_min_sync(0xffffffffu, xlo_);
+                const int xhi = __reduce_max_sync(0xffffffffu, xhi_);
                 LevelSched L;
                 L.first = n;
                 L.count = 0;
