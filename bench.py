@@ -54,6 +54,10 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="C2")
     ap.add_argument("--precision", default="fp16", choices=["fp32", "tf32", "bf16", "fp16", "fp32x3"])
+    ap.add_argument("--tile-order", default=None, choices=["source", "window_row", "auto"],
+                    help="how the fused kernel groups source pixels into tiles "
+                         "(dc_set_tile_order); default: auto for the backend workloads "
+                         "(large flow), source for the frontend")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-gpu", action="store_true")
     ap.add_argument("--scatter-mean", action="store_true",
@@ -233,6 +237,8 @@ def main():
     from slam_hands_b200 import configs
 
     wl = configs.WORKLOADS[args.workload]
+    if args.tile_order is None:
+        args.tile_order = "auto" if wl.mode == "alt" else "source"
     if args.impl == "reference":
         return run_reference_arm(args, wl)
     if args.scatter_mean:
@@ -277,6 +283,7 @@ def main():
     SPARES = 2
     dc = DroidCorrelation(wl.h, wl.w, channels=wl.channels, precision=args.precision,
                           alpha=wl.alpha, max_frames=wl.frames + SPARES, max_edges=M, device=dev)
+    dc.set_tile_order(args.tile_order)
     out = torch.empty(M, dc.out_channels, wl.h, wl.w, device=dev)
     # L2 flush between steps: READ a buffer twice the L2 size, so the cache is
     # left holding clean lines (a write flush would leave ~126 MB of dirty lines
@@ -691,6 +698,7 @@ def main():
                                + (", coords reprojected from poses + inverse depths in the step"
                                   if proj is not None else ""),
                    "alpha": wl.alpha, "l2": "flushed between steps (252 MB read)",
+                   "tile_order": args.tile_order,
                    "step": ("one keyframe arrives per step: packed into the spare store slot "
                             "(other ranks pull it from rank 0 over NVLink with the copy "
                             "engines) beside the step's kernel over the resident keyframe "

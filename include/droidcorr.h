@@ -354,6 +354,34 @@ int dc_debug_inject_stall(long long wait_limit_ns);
  * stream in the reference). */
 int dc_set_max_ctas(dc_ctx* ctx, int max_ctas);
 
+/* Order in which the fused tensor-core kernel (dc_build_and_lookup and the
+ * calls built on it, fp16 / bf16 / tf32 / fp32x3) groups an edge's source
+ * pixels into its 128-pixel tiles.  A tile multiplies its pixels against every
+ * target row that any of their windows touches, so the order sets how many
+ * target rows each tile streams:
+ *   DC_ORDER_SOURCE      128 consecutive source pixels (the default): compact
+ *                        when the flow is smooth, nearly the whole level when
+ *                        neighbouring pixels' windows scatter (large, noisy
+ *                        flow -- the backend's N(0, 8 px) graphs);
+ *   DC_ORDER_WINDOW_ROW  a pre-pass sorts each edge's pixels by the row of
+ *                        their level-0 window (stable, ties by pixel index); a
+ *                        tile's windows then share a few rows, at the price of
+ *                        scattered output stores and a gathered source tile;
+ *   DC_ORDER_AUTO        the pre-pass picks, per edge, the window-row order
+ *                        when it cuts the target rows summed over the edge's
+ *                        tiles at least 3 times, else the source order.
+ * Results do not depend on the order (each output is computed from its own
+ * pixel's dot products).  The first call with an order other than
+ * DC_ORDER_SOURCE allocates the permutation scratch (4 bytes per pixel and
+ * edge, max_edges edges); grids taller than 496 rows keep the source order.
+ * The pre-pass is one more launch per call, and calls on one context share
+ * the scratch (one call in flight per context).  No reference counterpart: the reference's volume
+ * build has no tiles (main.cu:1555-1613). */
+#define DC_ORDER_SOURCE 0
+#define DC_ORDER_WINDOW_ROW 1
+#define DC_ORDER_AUTO 2
+int dc_set_tile_order(dc_ctx* ctx, int order);
+
 /* Number of kernel launches the library has issued on this context (for
  * launch accounting in benchmarks). */
 long long dc_launch_count(const dc_ctx* ctx);

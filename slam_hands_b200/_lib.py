@@ -31,6 +31,12 @@ DC_PREC_FP32X3 = 4
 PRECISIONS = {"fp32": DC_PREC_FP32, "tf32": DC_PREC_TF32, "bf16": DC_PREC_BF16,
               "fp16": DC_PREC_FP16, "fp32x3": DC_PREC_FP32X3}
 
+DC_ORDER_SOURCE = 0
+DC_ORDER_WINDOW_ROW = 1
+DC_ORDER_AUTO = 2
+TILE_ORDERS = {"source": DC_ORDER_SOURCE, "window_row": DC_ORDER_WINDOW_ROW,
+               "auto": DC_ORDER_AUTO}
+
 DC_DTYPE_F32 = 0
 DC_DTYPE_F16 = 1
 
@@ -73,6 +79,7 @@ SIGNATURES = {
                                         _vp, _vp, _vp]),
     "dc_static_device_status": (_i, [_vp]),
     "dc_set_max_ctas": (_i, [_vp, _i]),
+    "dc_set_tile_order": (_i, [_vp, _i]),
     "dc_store_ipc_handle": (_i, [_vp, _vp]),
     "dc_store_attach_source": (_i, [_vp, _vp]),
     "dc_store_pull_slots": (_i, [_vp, _i, _i, _vp]),

@@ -110,6 +110,16 @@ class DroidCorrelation:
         free for work on other streams (dc_set_max_ctas)."""
         self._check(self.lib.dc_set_max_ctas(self._ctx, int(max_ctas)))
 
+    def set_tile_order(self, order: str) -> None:
+        """How the fused kernel groups each edge's source pixels into tiles
+        (dc_set_tile_order): "source" (consecutive pixels, the default),
+        "window_row" (sorted by the row of their level-0 window: fewer target
+        rows per tile under large, noisy flow) or "auto" (per edge, the window-row
+        order where it streams at least 3x fewer target rows)."""
+        if order not in L.TILE_ORDERS:
+            raise ValueError(f"order must be one of {sorted(L.TILE_ORDERS)}")
+        self._check(self.lib.dc_set_tile_order(self._ctx, L.TILE_ORDERS[order]))
+
     def set_frames(self, fmaps: torch.Tensor, first_slot: int = 0,
                    stream: Optional[torch.cuda.Stream] = None) -> None:
         """Pack fmaps [K, C, h, w] (fp32 or fp16) into slots first_slot..+K."""

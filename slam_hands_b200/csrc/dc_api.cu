@@ -170,6 +170,7 @@ int dc_destroy(dc_ctx* ctx) {
     if (ctx->store) cudaFree(ctx->store);
     if (ctx->dev_err) cudaFree(ctx->dev_err);
     if (ctx->enc_w) cudaFree(ctx->enc_w);
+    if (ctx->tile_perm) cudaFree(ctx->tile_perm);
     if (ctx->src_store) cudaIpcCloseMemHandle(ctx->src_store);
     if (prev >= 0) cudaSetDevice(prev);
     delete ctx;
@@ -186,6 +187,28 @@ int dc_set_max_ctas(dc_ctx* ctx, int max_ctas) {
     if (!ctx) return DC_ERR_INVALID_ARG;
     if (max_ctas < 0) return dc_fail(ctx, DC_ERR_INVALID_ARG, "max_ctas < 0");
     ctx->max_ctas = max_ctas;
+    return DC_OK;
+}
+
+int dc_set_tile_order(dc_ctx* ctx, int order) {
+    if (!ctx) return DC_ERR_INVALID_ARG;
+    if (order != DC_ORDER_SOURCE && order != DC_ORDER_WINDOW_ROW && order != DC_ORDER_AUTO)
+        return dc_fail(ctx, DC_ERR_INVALID_ARG, "order must be DC_ORDER_SOURCE, _WINDOW_ROW or _AUTO");
+    if (order != DC_ORDER_SOURCE && !ctx->tile_perm) {
+        // per edge: the permutation (hw), its flag (1), the permuted coordinates (2 hw)
+        const size_t words = (size_t)ctx->cfg.max_edges * (3 * (size_t)ctx->hw + 1);
+        int prev = -1;
+        cudaGetDevice(&prev);
+        cudaSetDevice(ctx->device);
+        const cudaError_t e = cudaMalloc(&ctx->tile_perm, words * sizeof(int));
+        if (prev >= 0) cudaSetDevice(prev);
+        if (e != cudaSuccess) {
+            ctx->tile_perm = nullptr;
+            cudaGetLastError();
+            return dc_fail(ctx, DC_ERR_NO_MEMORY, "tile permutation scratch");
+        }
+    }
+    ctx->tile_order = order;
     return DC_OK;
 }
 

@@ -46,6 +46,14 @@ struct dc_ctx {
     alignas(64) unsigned char tmap_b[DC_MAX_LEVELS][128];
     alignas(64) unsigned char tmap_b_lo[DC_MAX_LEVELS][128];  // DC_PREC_FP32X3: the lo copy
     bool tc_ready = false;
+    // fused kernel's tile order (dc_set_tile_order) and its scratch: the pixel
+    // permutation [max_edges][hw] (tile position -> source pixel), one flag per
+    // edge (1: permuted, 0: identity), the coordinates in tile-position order
+    // [max_edges][2][hw]
+    int tile_order = 0;
+    int* tile_perm = nullptr;
+    // 2-D map of the store with one-row boxes (row gathers of the source tile)
+    alignas(64) unsigned char tmap_a_rows[128];
     // correlation encoder (dc_set_corr_encoder): packed fp16 weights, then the bias
     void* enc_w = nullptr;
     bool enc_ready = false;

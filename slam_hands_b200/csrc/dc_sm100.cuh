@@ -112,6 +112,19 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, int 
         : "memory");
 }
 
+// Row gather global -> shared: rows r0..r3 of a 2-D map whose box is one row of
+// c0 .. c0 + box width - 1, written as four consecutive box rows at `dst` (the
+// map's swizzle applies by shared-memory address, as for a 4-row tile).
+__device__ __forceinline__ void tma_gather4(uint32_t dst, const void* tmap, int c0, int r0,
+                                            int r1, int r2, int r3, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(r0), "r"(r1), "r"(r2), "r"(r3),
+        "r"(bar)
+        : "memory");
+}
+
 // ---- tcgen05 -------------------------------------------------------------------
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(

@@ -130,6 +130,7 @@ __device__ __forceinline__ int div_small(int v, float inv_d) {
 struct TcMaps {
     CUtensorMap a;
     CUtensorMap b[DC_MAX_LEVELS];
+    CUtensorMap a_rows;  // the store with one-row boxes: source-tile row gathers
 };
 
 struct TcParams {
@@ -139,6 +140,11 @@ struct TcParams {
     const int* jj;
     int max_frames;
     const float* coords;
+    // window-row tile order (null: source order): tile position -> source pixel,
+    // per-edge flag (1: permuted), coordinates in tile-position order
+    const int* perm;
+    const int* pflag;
+    const float* pcoords;
     float* out;
     int* err;
     int atoms;        // 128-byte K atoms per operand row (C * 2 / 128)
@@ -152,11 +158,11 @@ struct TcParams {
 };
 
 struct TileInfo {
-    int e, p0, si, sj, n, valid, pad0, pad1;
+    int e, p0, si, sj, n, valid, gather, pad1;  // gather: source rows are permuted
 };
 
 struct Layout {
-    uint32_t a, b, stage_b, win, sched, tinfo, bars, misc, strips, reps, total;
+    uint32_t a, b, stage_b, win, sched, tinfo, bars, misc, strips, reps, rows, total;
 };
 
 __host__ __device__ constexpr Layout make_layout(int atoms) {
@@ -171,7 +177,8 @@ __host__ __device__ constexpr Layout make_layout(int atoms) {
     L.misc = L.bars + 24 * 8;
     L.strips = L.misc + 64;                                  // [levels][32] int
     L.reps = L.strips + DC_MAX_LEVELS * kChunkStrips * 4;    // [levels][33] uint
-    L.total = L.reps + DC_MAX_LEVELS * (kChunkStrips + 1) * 4;
+    L.rows = L.reps + DC_MAX_LEVELS * (kChunkStrips + 1) * 4;  // [128] u16: gathered pixels
+    L.total = L.rows + kTileM * 2;
     return L;
 }
 static_assert(make_layout(2).total + 1024 <= 227 * 1024, "shared memory budget");
@@ -401,19 +408,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         int gc = 0, na = 0, i = 0;
         int a_issued = 0, a_parity = 0, last_gc = 0;
         float cxn[kTileM / 32], cyn[kTileM / 32];
-        int sin_ = -1, sjn = -1;
+        int pxn[kTileM / 32];
+        int sin_ = -1, sjn = -1, gan = 0;
+        const float* const cbase = P.perm ? P.pcoords : P.coords;
+        unsigned short* const arows = reinterpret_cast<unsigned short*>(base + Ly.rows);
 #define DC_TC_LOAD_COORDS(tt)                                                      \
     do {                                                                           \
-        _Pragma("unroll") for (int k = 0; k < kTileM / 32; k++) cxn[k] = cyn[k] = 0.0f; \
+        _Pragma("unroll") for (int k = 0; k < kTileM / 32; k++) {                  \
+            cxn[k] = cyn[k] = 0.0f;                                                \
+            pxn[k] = 0;                                                            \
+        }                                                                          \
         if ((tt) < ntiles) {                                                       \
             const int e_ = (tt) / tpe, q0_ = ((tt) - e_ * tpe) * kTileM;           \
             sin_ = __ldg(P.ii + e_);                                               \
             sjn = __ldg(P.jj + e_);                                                \
+            gan = P.perm ? __ldg(P.pflag + e_) : 0;                                \
             _Pragma("unroll") for (int k = 0; k < kTileM / 32; k++) {              \
                 const int q_ = q0_ + lane + 32 * k;                                \
                 if (q_ < hw) {                                                     \
-                    cxn[k] = __ldg(P.coords + (size_t)e_ * 2 * hw + q_);           \
-                    cyn[k] = __ldg(P.coords + (size_t)e_ * 2 * hw + hw + q_);      \
+                    cxn[k] = __ldg(cbase + (size_t)e_ * 2 * hw + q_);              \
+                    cyn[k] = __ldg(cbase + (size_t)e_ * 2 * hw + hw + q_);         \
+                    if (P.perm) pxn[k] = __ldg(P.perm + (size_t)e_ * hw + q_);     \
                 }                                                                  \
             }                                                                      \
         }                                                                          \
@@ -426,10 +441,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
             float cx[kTileM / 32], cy[kTileM / 32];
+            const int ga = gan;
 #pragma unroll
             for (int k = 0; k < kTileM / 32; k++) {
                 cx[k] = cxn[k];
                 cy[k] = cyn[k];
+                // the source rows to gather (read by lane 0 in the issue loop below)
+                if (ga) arows[lane + 32 * k] = (unsigned short)pxn[k];  // hw <= DC_MAX_HW < 2^16
             }
             const int si = sin_, sj = sjn;
             DC_TC_LOAD_COORDS(t + gridDim.x);
@@ -491,7 +509,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ti.sj = sj;
                 ti.n = n;
                 ti.valid = valid;
-                ti.pad0 = ti.pad1 = 0;
+                ti.gather = ga;
+                ti.pad1 = 0;
                 tinfo[tb] = ti;
             }
             __syncwarp();
@@ -513,11 +532,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                         if (!(P.stall && na == 0)) {
                             mbar_arrive_expect_tx(bar(kBarAFull), P.atoms * kTileM * kRowBytes);
-                            const int arow =
-                                (int)((long long)ti.si * g.frame_rows + P.a_off + g.row0[0] + ti.p0);
-                            for (int k = 0; k < P.atoms; k++)
-                                tma_load_2d(sA + k * kTileM * kRowBytes, &maps.a, k * 64, arow,
-                                            bar(kBarAFull));
+                            const int rbase =
+                                (int)((long long)ti.si * g.frame_rows + P.a_off + g.row0[0]);
+                            if (ti.gather) {
+                                // permuted tile: 4 source rows per gather (512 bytes)
+                                for (int k = 0; k < P.atoms; k++)
+#pragma unroll 1
+                                    for (int j = 0; j < kTileM / 4; j++)
+                                        tma_gather4(sA + k * kTileM * kRowBytes + j * 4 * kRowBytes,
+                                                    &maps.a_rows, k * 64, rbase + arows[4 * j],
+                                                    rbase + arows[4 * j + 1], rbase + arows[4 * j + 2],
+                                                    rbase + arows[4 * j + 3], bar(kBarAFull));
+                            } else {
+                                for (int k = 0; k < P.atoms; k++)
+                                    tma_load_2d(sA + k * kTileM * kRowBytes, &maps.a, k * 64,
+                                                rbase + ti.p0, bar(kBarAFull));
+                            }
                             a_issued = 1;
                             a_parity = na & 1;
                         }
@@ -546,6 +576,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (ti.n > 0) na++;
             __syncwarp();
         }
+        (void)arows;
         if (lane == 0) {
             DC_PROF_STORE(4, w_a);
             if (*abort) {
@@ -646,15 +677,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         int gc = 0, i = 0;
         bool alive = true;
         // this pixel's coordinates, loaded one tile ahead
+        // (window-row order: the coordinates in tile-position order; outputs are
+        // written at the tile position and moved to their pixel by
+        // unpermute_rows_kernel after the call's passes)
         float cx_next = 0.0f, cy_next = 0.0f;
+        const float* const cbase = P.perm ? P.pcoords : P.coords;
 #define DC_TC_PIXEL_COORDS(tt)                                               \
     do {                                                                     \
         cx_next = cy_next = 0.0f;                                            \
         if ((tt) < ntiles) {                                                 \
             const int e_ = (tt) / tpe, q_ = ((tt) - e_ * tpe) * kTileM + ti_px; \
             if (q_ < hw) {                                                   \
-                cx_next = __ldg(P.coords + (size_t)e_ * 2 * hw + q_);        \
-                cy_next = __ldg(P.coords + (size_t)e_ * 2 * hw + hw + q_);   \
+                cx_next = __ldg(cbase + (size_t)e_ * 2 * hw + q_);           \
+                cy_next = __ldg(cbase + (size_t)e_ * 2 * hw + hw + q_);      \
             }                                                                \
         }                                                                    \
     } while (0)
@@ -671,7 +706,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             w_a += DC_PROF_NOW() - t0s;
             const TileInfo tinf = tinfo[tb];
             const LevelSched* sch = sched_base + tb * DC_MAX_LEVELS;
-            const int p = tinf.p0 + ti_px;
+            const int p = tinf.p0 + ti_px;  // tile position = pixel in source order
             const bool pv = p < hw;
             const bool valid = tinf.valid != 0;
             float* out_e = P.out + (size_t)tinf.e * nch * hw;
@@ -787,6 +822,162 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) DC_PROF_STORE(0, DC_PROF_NOW() - t_start);
 }
 
+// ---- window-row tile order (dc_set_tile_order) -------------------------------
+// One CTA per edge sorts the edge's source pixels by the row of their level-0
+// window, key = floor(y) clamped to [-kBinPad, H0 + kBinPad - 1]: a counting
+// sort, stable (ties in pixel order), deterministic.  Warp w owns a contiguous
+// segment of pixels; cnt[key][w] counts, an exclusive scan in (key, warp) order
+// turns the counts into each warp's first position per key, and each warp then
+// places its pixels in order (__match_any_sync ranks equal keys within 32).
+// The kernel also estimates, for both orders, the target rows the fused kernel
+// would stream (per 128-pixel tile: key span + 2r + 2) and, for DC_ORDER_AUTO,
+// keeps the window-row order only where it cuts that sum kAutoGain times.  It
+// writes the permutation, the flag, and the coordinates in position order.
+constexpr int kBinThreads = 1024;
+constexpr int kBinPad = 8;
+constexpr int kBinMaxKeys = 512;
+// DC_ORDER_AUTO keeps the window-row order where it cuts the estimated target
+// rows at least this many times: measured on one B200, a 1.8x cut (48x64, flow
+// noise N(0, 2 px)) made the call 1.5x slower (the pre-pass, the gathered
+// source tiles and the output reordering cost more than the rows saved), a
+// 4.8x cut (54x96, N(0, 8 px)) made it 1.4x faster.
+constexpr int kAutoGain = 3;
+
+__device__ __forceinline__ int bin_key(float y, int H0) {
+    // fmaxf / fminf return the other operand for a NaN: NaN sorts first
+    const float yc = fminf(fmaxf(y, -(float)kBinPad), (float)(H0 + kBinPad - 1));
+    return (int)floorf(yc) + kBinPad;
+}
+
+__global__ void __launch_bounds__(kBinThreads)
+    tile_order_kernel(const float* coords, int hw, int H0, int R, int order, int* perm,
+                      int* pflag, float* pcoords) {
+    extern __shared__ int cnt[];  // [nkeys][32]
+    __shared__ int warp_tot[32];
+    __shared__ int cost[2];       // target rows summed over tiles: source, window-row order
+    const int e = blockIdx.x, nkeys = H0 + 2 * kBinPad;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float* cx = coords + (size_t)e * 2 * hw;
+    const float* cy = cx + hw;
+    int* pe = perm + (size_t)e * hw;
+    float* qx = pcoords + (size_t)e * 2 * hw;
+    float* qy = qx + hw;
+    const int seg = ((hw + 31) / 32 + 31) & ~31;  // pixels per warp, a multiple of 32
+    const int beg = min(warp * seg, hw), end = min(beg + seg, hw);
+    const int ntile = (hw + 127) / 128;
+    for (int i = threadIdx.x; i < nkeys * 32; i += kBinThreads) cnt[i] = 0;
+    if (threadIdx.x < 2) cost[threadIdx.x] = 0;
+    __syncthreads();
+    for (int p = beg + lane; p < end; p += 32) atomicAdd(&cnt[bin_key(cy[p], H0) * 32 + warp], 1);
+    for (int t = warp; t < ntile; t += 32) {
+        int lo = 0x7fffffff, hi = -1;
+        for (int k = 0; k < 4; k++) {
+            const int p = 128 * t + lane + 32 * k;
+            if (p < hw) {
+                const int key = bin_key(cy[p], H0);
+                lo = min(lo, key);
+                hi = max(hi, key);
+            }
+        }
+        lo = __reduce_min_sync(0xffffffffu, lo);
+        hi = __reduce_max_sync(0xffffffffu, hi);
+        if (lane == 0) atomicAdd(&cost[0], hi - lo + 2 * R + 2);
+    }
+    __syncthreads();
+    // exclusive scan of cnt in (key, warp) order: per thread a run of entries
+    const int n = nkeys * 32, per = (n + kBinThreads - 1) / kBinThreads;
+    const int i0 = min(threadIdx.x * per, n), i1 = min(i0 + per, n);
+    int run_sum = 0;
+    for (int i = i0; i < i1; i++) run_sum += cnt[i];
+    int inc = run_sum;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, inc, d);
+        if (lane >= d) inc += v;
+    }
+    if (lane == 31) warp_tot[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {
+        const int v = warp_tot[lane];
+        int wi = v;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const int u = __shfl_up_sync(0xffffffffu, wi, d);
+            if (lane >= d) wi += u;
+        }
+        warp_tot[lane] = wi - v;
+    }
+    __syncthreads();
+    int run = warp_tot[warp] + inc - run_sum;
+    for (int i = i0; i < i1; i++) {
+        const int c = cnt[i];
+        cnt[i] = run;
+        run += c;
+    }
+    __syncthreads();
+    // key of sorted position s: the last key whose first position is <= s
+    auto key_at = [&](int s_) {
+        int lo = 0, hi = nkeys - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (cnt[mid * 32] <= s_) lo = mid; else hi = mid - 1;
+        }
+        return lo;
+    };
+    for (int t = threadIdx.x; t < ntile; t += kBinThreads) {
+        const int s0 = 128 * t, s1 = min(s0 + 128, hw) - 1;
+        atomicAdd(&cost[1], key_at(s1) - key_at(s0) + 2 * R + 2);
+    }
+    __syncthreads();
+    const bool binned = order == DC_ORDER_WINDOW_ROW ||
+                        (order == DC_ORDER_AUTO && kAutoGain * cost[1] <= cost[0]);
+    if (threadIdx.x == 0) pflag[e] = binned ? 1 : 0;
+    if (!binned) {
+        for (int p = threadIdx.x; p < hw; p += kBinThreads) {
+            pe[p] = p;
+            qx[p] = cx[p];
+            qy[p] = cy[p];
+        }
+        return;
+    }
+    for (int p0 = beg; p0 < end; p0 += 32) {
+        const int p = p0 + lane;
+        const bool act = p < end;
+        const unsigned am = __ballot_sync(0xffffffffu, act);
+        if (act) {
+            const float y = cy[p];
+            const int key = bin_key(y, H0);
+            const unsigned peers = __match_any_sync(am, key);
+            const int rank = __popc(peers & ((1u << lane) - 1u));
+            int* slot = &cnt[key * 32 + warp];
+            const int pos = *slot + rank;
+            pe[pos] = p;
+            qx[pos] = cx[p];
+            qy[pos] = y;
+            __syncwarp(am);
+            if (rank == 0) *slot += __popc(peers);
+        }
+        __syncwarp();
+    }
+}
+
+// Window-row order, after the fused kernel: row (e, ch) of `out` holds its
+// values in tile-position order; move them to pixel order in place (one CTA
+// per row: the row through shared memory, so that both global passes are
+// coalesced).  Rows of edges left in source order (flag 0) are skipped.
+constexpr int kUnpermThreads = 256;
+__global__ void __launch_bounds__(kUnpermThreads)
+    unpermute_rows_kernel(float* out, int nch, int hw, const int* perm, const int* pflag) {
+    extern __shared__ float row_s[];  // [hw], pixel order
+    const int e = blockIdx.x / nch;
+    if (!__ldg(pflag + e)) return;
+    float* row = out + (size_t)blockIdx.x * hw;
+    const int* pe = perm + (size_t)e * hw;
+    for (int s_ = threadIdx.x; s_ < hw; s_ += kUnpermThreads) row_s[__ldg(pe + s_)] = __ldcs(row + s_);
+    __syncthreads();
+    for (int p = threadIdx.x; p < hw; p += kUnpermThreads) __stcs(row + p, row_s[p]);
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
@@ -868,6 +1059,13 @@ int dc_tc_prepare(dc_ctx* ctx) {
                       CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r1 != CUDA_SUCCESS) return dc_fail(ctx, DC_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+    cuuint32_t box_row[2] = {64, 1};
+    CUresult r2 = enc(reinterpret_cast<CUtensorMap*>(ctx->tmap_a_rows), dt, 2, ctx->store, dims,
+                      strides, box_row, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r2 != CUDA_SUCCESS)
+        return dc_fail(ctx, DC_ERR_CUDA, "cuTensorMapEncodeTiled (row gathers) failed");
     for (int l = 0; l < ctx->cfg.levels * (ctx->lo_rows > 0 ? 2 : 1); l++) {
         const bool lo = l >= ctx->cfg.levels;  // FP32X3: maps of the lo copy
         const int lv = lo ? l - ctx->cfg.levels : l;
@@ -902,6 +1100,9 @@ int dc_launch_tc(dc_ctx* ctx, const int* ii, const int* jj, int M, const float* 
     P.jj = jj;
     P.max_frames = ctx->cfg.max_frames;
     P.coords = coords;
+    P.perm = nullptr;
+    P.pflag = nullptr;
+    P.pcoords = nullptr;
     P.out = out;
     P.err = ctx->dev_err;
     P.atoms = ctx->cfg.channels * 2 / 128;
@@ -912,6 +1113,21 @@ int dc_launch_tc(dc_ctx* ctx, const int* ii, const int* jj, int M, const float* 
     const long long lim = g_test_wait_ns.load();
     P.stall = lim > 0;
     P.wait_ns = lim > 0 ? (unsigned long long)lim : 2000000000ull;
+    const int nkeys = ctx->H[0] + 2 * kBinPad;
+    if (ctx->tile_order != DC_ORDER_SOURCE && ctx->tile_perm && M > 0 && nkeys <= kBinMaxKeys) {
+        const size_t me = (size_t)ctx->cfg.max_edges, nhw = (size_t)ctx->hw;
+        P.perm = ctx->tile_perm;
+        P.pflag = ctx->tile_perm + me * nhw;
+        P.pcoords = reinterpret_cast<const float*>(ctx->tile_perm + me * nhw + me);
+        const int bsm = nkeys * 32 * (int)sizeof(int);
+        cudaFuncSetAttribute(tile_order_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bsm);
+        tile_order_kernel<<<M, kBinThreads, bsm, s>>>(coords, ctx->hw, ctx->H[0], ctx->cfg.radius,
+                                                      ctx->tile_order, ctx->tile_perm,
+                                                      ctx->tile_perm + me * nhw,
+                                                      const_cast<float*>(P.pcoords));
+        const int rcb = dc_check_launch(ctx, "tile_order_kernel");
+        if (rcb) return rcb;
+    }
     const Layout Ly = make_layout(P.atoms);
     const size_t smem = Ly.total + 1024;
     const int ntiles = (ctx->hw + kTileM - 1) / kTileM * M;
@@ -927,6 +1143,7 @@ int dc_launch_tc(dc_ctx* ctx, const int* ii, const int* jj, int M, const float* 
         TcMaps maps;
         memset(&maps, 0, sizeof(maps));
         memcpy(&maps.a, ctx->tmap_a, sizeof(CUtensorMap));
+        memcpy(&maps.a_rows, ctx->tmap_a_rows, sizeof(CUtensorMap));
         for (int l = 0; l < ctx->cfg.levels; l++)
             memcpy(&maps.b[l], b_lo ? ctx->tmap_b_lo[l] : ctx->tmap_b[l], sizeof(CUtensorMap));
 #define DC_TC_LAUNCH(RR)                                                                 \
@@ -943,6 +1160,15 @@ int dc_launch_tc(dc_ctx* ctx, const int* ii, const int* jj, int M, const float* 
         }
 #undef DC_TC_LAUNCH
         const int rc = dc_check_launch(ctx, "corr_tc_kernel");
+        if (rc) return rc;
+    }
+    if (P.perm) {
+        const int nch = ctx->cfg.levels * (2 * ctx->cfg.radius + 1) * (2 * ctx->cfg.radius + 1);
+        const int usm = ctx->hw * (int)sizeof(float);
+        cudaFuncSetAttribute(unpermute_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, usm);
+        unpermute_rows_kernel<<<M * nch, kUnpermThreads, usm, s>>>(out, nch, ctx->hw, P.perm,
+                                                                   P.pflag);
+        const int rc = dc_check_launch(ctx, "unpermute_rows_kernel");
         if (rc) return rc;
     }
     return DC_OK;
