@@ -58,6 +58,9 @@ def parse():
                     help="how the fused kernel groups source pixels into tiles "
                          "(dc_set_tile_order); default: auto for the backend workloads "
                          "(large flow), source for the frontend")
+    ap.add_argument("--edges", type=int, default=0,
+                    help="profiling only: keep the first N edges of a backend workload "
+                         "(a small case for multi-pass ncu captures); not a bench line")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-gpu", action="store_true")
     ap.add_argument("--scatter-mean", action="store_true",
@@ -269,6 +272,8 @@ def main():
     if not frontend:
         a, b = edge_range(len(ii0), world, rank)
         ii, jj, coords = ii0[a:b], jj0[a:b], coords[a:b].contiguous()
+        if args.edges > 0:
+            ii, jj, coords = ii[:args.edges], jj[:args.edges], coords[:args.edges].contiguous()
     else:
         ii, jj = configs.make_edges(wl, seed=configs.SEED + 101 * rank) if rank else (ii0, jj0)
     M = len(ii)
@@ -699,6 +704,8 @@ def main():
                                   if proj is not None else ""),
                    "alpha": wl.alpha, "l2": "flushed between steps (252 MB read)",
                    "tile_order": args.tile_order,
+                   **({"edges_cap": args.edges, "valid": "profiling case, not a bench line"}
+                      if args.edges > 0 else {}),
                    "step": ("one keyframe arrives per step: packed into the spare store slot "
                             "(other ranks pull it from rank 0 over NVLink with the copy "
                             "engines) beside the step's kernel over the resident keyframe "

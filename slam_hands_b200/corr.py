@@ -115,7 +115,7 @@ class DroidCorrelation:
         (dc_set_tile_order): "source" (consecutive pixels, the default),
         "window_row" (sorted by the row of their level-0 window: fewer target
         rows per tile under large, noisy flow) or "auto" (per edge, the window-row
-        order where it streams at least 3x fewer target rows)."""
+        order where it saves enough target pixels per tile)."""
         if order not in L.TILE_ORDERS:
             raise ValueError(f"order must be one of {sorted(L.TILE_ORDERS)}")
         self._check(self.lib.dc_set_tile_order(self._ctx, L.TILE_ORDERS[order]))

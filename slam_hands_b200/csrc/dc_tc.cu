@@ -831,17 +831,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 // places its pixels in order (__match_any_sync ranks equal keys within 32).
 // The kernel also estimates, for both orders, the target rows the fused kernel
 // would stream (per 128-pixel tile: key span + 2r + 2) and, for DC_ORDER_AUTO,
-// keeps the window-row order only where it cuts that sum kAutoGain times.  It
+// keeps the window-row order only where it saves enough (kAutoPxPerChannel).  It
 // writes the permutation, the flag, and the coordinates in position order.
 constexpr int kBinThreads = 1024;
 constexpr int kBinPad = 8;
 constexpr int kBinMaxKeys = 512;
-// DC_ORDER_AUTO keeps the window-row order where it cuts the estimated target
-// rows at least this many times: measured on one B200, a 1.8x cut (48x64, flow
-// noise N(0, 2 px)) made the call 1.5x slower (the pre-pass, the gathered
-// source tiles and the output reordering cost more than the rows saved), a
-// 4.8x cut (54x96, N(0, 8 px)) made it 1.4x faster.
-constexpr int kAutoGain = 3;
+// DC_ORDER_AUTO keeps the window-row order where the level-0 target pixels it
+// saves per 128-pixel tile (estimated rows saved x W0) reach kAutoPxPerChannel
+// x the output channels: the gain grows with the target pixels no longer
+// multiplied, the cost (reordering the tile's outputs, one read and one write
+// of 128 x channels floats) with the channels.  Measured on one B200 (fp16,
+// 196 channels, so a threshold of 3136): ~530 pixels saved per tile (48x64,
+// flow noise N(0, 2 px)): 1.5x slower; ~2200 (48x64, N(0, 8 px)): 3 % slower;
+// ~3500 (54x96, N(0, 8 px)): 1.4x faster.
+constexpr int kAutoPxPerChannel = 16;
 
 __device__ __forceinline__ int bin_key(float y, int H0) {
     // fmaxf / fminf return the other operand for a NaN: NaN sorts first
@@ -850,8 +853,8 @@ __device__ __forceinline__ int bin_key(float y, int H0) {
 }
 
 __global__ void __launch_bounds__(kBinThreads)
-    tile_order_kernel(const float* coords, int hw, int H0, int R, int order, int* perm,
-                      int* pflag, float* pcoords) {
+    tile_order_kernel(const float* coords, int hw, int H0, int W0, int nch, int R, int order,
+                      int* perm, int* pflag, float* pcoords) {
     extern __shared__ int cnt[];  // [nkeys][32]
     __shared__ int warp_tot[32];
     __shared__ int cost[2];       // target rows summed over tiles: source, window-row order
@@ -930,7 +933,9 @@ __global__ void __launch_bounds__(kBinThreads)
     }
     __syncthreads();
     const bool binned = order == DC_ORDER_WINDOW_ROW ||
-                        (order == DC_ORDER_AUTO && kAutoGain * cost[1] <= cost[0]);
+                        (order == DC_ORDER_AUTO &&
+                         (long long)(cost[0] - cost[1]) * W0 >=
+                             (long long)kAutoPxPerChannel * nch * ntile);
     if (threadIdx.x == 0) pflag[e] = binned ? 1 : 0;
     if (!binned) {
         for (int p = threadIdx.x; p < hw; p += kBinThreads) {
@@ -964,18 +969,45 @@ __global__ void __launch_bounds__(kBinThreads)
 // Window-row order, after the fused kernel: row (e, ch) of `out` holds its
 // values in tile-position order; move them to pixel order in place (one CTA
 // per row: the row through shared memory, so that both global passes are
-// coalesced).  Rows of edges left in source order (flag 0) are skipped.
+// coalesced).  A CTA takes kUnpermRows rows of one edge (grid: edges x row
+// groups), so the CTAs of edges left in source order (flag 0), which return at
+// once, are few.
 constexpr int kUnpermThreads = 256;
+constexpr int kUnpermRows = 7;
 __global__ void __launch_bounds__(kUnpermThreads)
     unpermute_rows_kernel(float* out, int nch, int hw, const int* perm, const int* pflag) {
     extern __shared__ float row_s[];  // [hw], pixel order
-    const int e = blockIdx.x / nch;
+    const int e = blockIdx.x;
     if (!__ldg(pflag + e)) return;
-    float* row = out + (size_t)blockIdx.x * hw;
     const int* pe = perm + (size_t)e * hw;
-    for (int s_ = threadIdx.x; s_ < hw; s_ += kUnpermThreads) row_s[__ldg(pe + s_)] = __ldcs(row + s_);
-    __syncthreads();
-    for (int p = threadIdx.x; p < hw; p += kUnpermThreads) __stcs(row + p, row_s[p]);
+    const int ch1 = min(nch, (int)(blockIdx.y + 1) * kUnpermRows);
+    for (int ch = blockIdx.y * kUnpermRows; ch < ch1; ch++) {
+        float* row = out + ((size_t)e * nch + ch) * hw;
+        __syncthreads();  // the previous row's stores have read row_s
+        if ((hw & 3) == 0) {
+            // rows start 16-byte aligned: 4 values (and 4 pixel indices) per access
+            const int n4 = hw >> 2;
+            const float4* row4 = reinterpret_cast<const float4*>(row);
+            const int4* pe4 = reinterpret_cast<const int4*>(pe);
+            for (int i = threadIdx.x; i < n4; i += kUnpermThreads) {
+                const float4 v = __ldcs(row4 + i);
+                const int4 q = __ldg(pe4 + i);
+                row_s[q.x] = v.x;
+                row_s[q.y] = v.y;
+                row_s[q.z] = v.z;
+                row_s[q.w] = v.w;
+            }
+            __syncthreads();
+            float4* out4 = reinterpret_cast<float4*>(row);
+            for (int i = threadIdx.x; i < n4; i += kUnpermThreads)
+                __stcs(out4 + i, reinterpret_cast<const float4*>(row_s)[i]);
+        } else {
+            for (int s_ = threadIdx.x; s_ < hw; s_ += kUnpermThreads)
+                row_s[__ldg(pe + s_)] = __ldcs(row + s_);
+            __syncthreads();
+            for (int p = threadIdx.x; p < hw; p += kUnpermThreads) __stcs(row + p, row_s[p]);
+        }
+    }
 }
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -1121,7 +1153,9 @@ int dc_launch_tc(dc_ctx* ctx, const int* ii, const int* jj, int M, const float* 
         P.pcoords = reinterpret_cast<const float*>(ctx->tile_perm + me * nhw + me);
         const int bsm = nkeys * 32 * (int)sizeof(int);
         cudaFuncSetAttribute(tile_order_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bsm);
-        tile_order_kernel<<<M, kBinThreads, bsm, s>>>(coords, ctx->hw, ctx->H[0], ctx->cfg.radius,
+        const int nch_o = ctx->cfg.levels * (2 * ctx->cfg.radius + 1) * (2 * ctx->cfg.radius + 1);
+        tile_order_kernel<<<M, kBinThreads, bsm, s>>>(coords, ctx->hw, ctx->H[0], ctx->W[0],
+                                                      nch_o, ctx->cfg.radius,
                                                       ctx->tile_order, ctx->tile_perm,
                                                       ctx->tile_perm + me * nhw,
                                                       const_cast<float*>(P.pcoords));
@@ -1166,8 +1200,8 @@ int dc_launch_tc(dc_ctx* ctx, const int* ii, const int* jj, int M, const float* 
         const int nch = ctx->cfg.levels * (2 * ctx->cfg.radius + 1) * (2 * ctx->cfg.radius + 1);
         const int usm = ctx->hw * (int)sizeof(float);
         cudaFuncSetAttribute(unpermute_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, usm);
-        unpermute_rows_kernel<<<M * nch, kUnpermThreads, usm, s>>>(out, nch, ctx->hw, P.perm,
-                                                                   P.pflag);
+        const dim3 ugrid(M, (nch + kUnpermRows - 1) / kUnpermRows);
+        unpermute_rows_kernel<<<ugrid, kUnpermThreads, usm, s>>>(out, nch, ctx->hw, P.perm, P.pflag);
         const int rc = dc_check_launch(ctx, "unpermute_rows_kernel");
         if (rc) return rc;
     }
