@@ -61,6 +61,8 @@ def parse():
     ap.add_argument("--edges", type=int, default=0,
                     help="profiling only: keep the first N edges of a backend workload "
                          "(a small case for multi-pass ncu captures); not a bench line")
+    ap.add_argument("--encoder", action="store_true",
+                    help="time dc_corr_encode (corr encoder first layer) at the workload's sizes instead")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-gpu", action="store_true")
     ap.add_argument("--scatter-mean", action="store_true",
@@ -235,6 +237,49 @@ def run_scatter_mean(args, wl):
     return 0
 
 
+def run_encoder(args, wl):
+    """The corr encoder's first layer alone (dc_corr_encode) on one batch of the
+    workload: M = its edges, 196 fp32 channels in, 128 fp16 channels out,
+    seeded features and weights.  Prints one JSON line with the CUDA-event time
+    (median of `steps`, L2 flushed between calls) and HBM GB/s on its
+    algorithmic bytes (features read once, outputs written once)."""
+    from slam_hands_b200 import DroidCorrelation
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    M = wl.edges if wl.mode != "alt" else 48
+    dc = DroidCorrelation(wl.h, wl.w, max_frames=2, max_edges=M, device=dev)
+    g = torch.Generator(device=dev).manual_seed(20261202)
+    corr = torch.randn(M, dc.out_channels, wl.h, wl.w, device=dev, generator=g)
+    w = torch.randn(128, dc.out_channels, device=dev, generator=g) / 14.0
+    b = torch.randn(128, device=dev, generator=g) * 0.1
+    dc.set_corr_encoder(w, b)
+    out = torch.empty(M, 128, wl.h, wl.w, dtype=torch.float16, device=dev)
+    flush = torch.empty(2 * L2_BYTES // 4, device=dev)
+    for _ in range(max(args.warmup, 3)):
+        dc.corr_encode(corr, out=out)
+    ts = []
+    for _ in range(args.steps):
+        flush.add_(1.0)
+        a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        dc.corr_encode(corr, out=out)
+        e.record()
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(e))
+    ms = statistics.median(ts)
+    byts = corr.numel() * 4 + out.numel() * 2
+    peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    peak, src = 6650.0, "fallback"
+    if os.path.exists(peaks_path):
+        peak, src = float(json.load(open(peaks_path))["hbm_gbs"]), "measured"
+    gbs = byts / (ms * 1e-3) / 1e9
+    print(json.dumps({"kernel": "dc_corr_encode", "workload": wl.name, "M": M,
+                      "ms_per_call": ms, "alg_bytes": byts, "GBs": gbs, "frac": gbs / peak,
+                      "peak_source": src}))
+    return 0
+
+
 def main():
     args = parse()
     from slam_hands_b200 import configs
@@ -246,6 +291,8 @@ def main():
         return run_reference_arm(args, wl)
     if args.scatter_mean:
         return run_scatter_mean(args, wl)
+    if args.encoder:
+        return run_encoder(args, wl)
 
     from slam_hands_b200 import DroidCorrelation
     from slam_hands_b200.shard import SlotRing, edge_range, peers_alive, replicate_store

@@ -18,9 +18,15 @@
 // accumulator; each warp reads 32 outputs of its lane quarter's 32 pixels back
 // (tcgen05.ld), adds the bias, applies the ReLU, rounds to fp16 and stores
 // 64-byte rows.
-// The wait for the MMAs is bounded (2 s) and reports through the context's
-// device error word.
+// That kernel serves grids whose h*w is not a multiple of 8; for the others
+// corr_encoder_tma_kernel streams the features with TMA (below).
+// The waits for the MMAs and the boxes are bounded (2 s) and report through
+// the context's device error word.
+#include <cuda.h>
 #include <cuda_fp16.h>
+
+#include <cstdint>
+#include <cstring>
 
 #include "dc_internal.cuh"
 #include "dc_sm100.cuh"
@@ -183,6 +189,184 @@ __global__ void __launch_bounds__(kEncThreads, 1) corr_encoder_kernel(EncParams 
     }
 }
 
+// The same layer with the feature tile streamed by TMA (h*w a multiple of 8,
+// features 16-byte aligned): one thread keeps kEncStages boxes of 64 channels
+// x 128 pixels fp32 (32 KB) in flight in a shared-memory ring, so the next
+// tile's loads overlap this tile's conversion, MMAs and stores.  All threads
+// convert a landed box into the fp16 K-major operand (4 threads per pixel row,
+// one 16-byte chunk of 8 channels each per pass); the last box of a tile holds
+// the remaining channels rounded up to 16 (rows past the channels, which
+// belong to the next edge or lie outside the tensor, are written as zeros).
+// Only the K steps that hold channels are issued.  Outputs are staged as fp16
+// [co][128 pixels] in the consumed operand tile and stored as 16-byte runs.
+constexpr int kEncStages = 3;
+constexpr uint32_t kStageBytes = 64u * kEncM * 4u;
+
+struct EncTmaParams {
+    const uint4* wimg;
+    const float* bias;
+    __half* out;
+    int* err;
+    int M, ci, hw;
+    int nfull;      // 64-channel boxes per tile
+    int tail_rows;  // channels of the last box, a multiple of 16 (0: none)
+};
+
+__global__ void __launch_bounds__(kEncThreads, 1)
+    corr_encoder_tma_kernel(const __grid_constant__ CUtensorMap mfull,
+                            const __grid_constant__ CUtensorMap mtail, EncTmaParams P) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    uint8_t* sB = base;                          // weights
+    uint8_t* sA = base + kWeightBytes;           // fp16 pixel tile / output staging
+    uint8_t* ring = sA + kOperandBytes;          // kEncStages fp32 boxes
+    uint64_t* bars = reinterpret_cast<uint64_t*>(ring + kEncStages * kStageBytes);
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + kEncStages + 1);
+    float* sbias = reinterpret_cast<float*>(ring + kEncStages * kStageBytes + 64);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int hw = P.hw;
+    const int tpe = (hw + kEncM - 1) / kEncM;
+    const int ntiles = tpe * P.M;
+    const int cpt = P.nfull + (P.tail_rows > 0 ? 1 : 0);  // boxes per tile
+    const int my_tiles = (int)blockIdx.x < ntiles ? (ntiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int nchunks = my_tiles * cpt;
+    const uint32_t mma_bar = smem_addr(bars + kEncStages);
+    const int ksteps = (P.ci + 15) / 16;
+
+    for (int i = tid; i < (int)(kWeightBytes / 16); i += kEncThreads)
+        reinterpret_cast<uint4*>(sB)[i] = __ldg(P.wimg + i);
+    if (tid < kEncCo) sbias[tid] = __ldg(P.bias + tid);
+    if (tid == 0) {
+        for (int st = 0; st <= kEncStages; st++) mbar_init(smem_addr(bars + st), 1);
+        fence_mbar_init();
+        tma_prefetch_desc(&mfull);
+        tma_prefetch_desc(&mtail);
+    }
+    if (warp == 0) {
+        tmem_alloc(smem_addr(tslot), 128);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+    const uint32_t idesc = idesc_f16(0u, kEncM, kEncCo);
+    const uint32_t aA = smem_addr(sA), aB = smem_addr(sB);
+
+    // box g of this CTA: tile blockIdx.x + (g / cpt) * gridDim.x, box g % cpt
+    int issued = 0;  // (thread 0)
+    auto issue = [&](int gi) {
+        const int t = (int)blockIdx.x + (gi / cpt) * (int)gridDim.x, c = gi % cpt;
+        const int e = t / tpe, p0 = (t - e * tpe) * kEncM;
+        const int st = gi % kEncStages;
+        const bool tail = c == P.nfull;
+        mbar_arrive_expect_tx(smem_addr(bars + st), (tail ? P.tail_rows : 64) * kEncM * 4u);
+        tma_load_2d(smem_addr(ring + st * kStageBytes), tail ? (const void*)&mtail : (const void*)&mfull,
+                    p0, e * P.ci + 64 * c, smem_addr(bars + st));
+        issued = gi + 1;
+    };
+    if (tid == 0)
+        for (int gi = 0; gi < min(kEncStages, nchunks); gi++) issue(gi);
+
+    int g = 0, mphase = 0;
+    bool alive = true, mma_out = false;
+    for (int t = blockIdx.x; t < ntiles && alive; t += gridDim.x, mphase ^= 1) {
+        const int e = t / tpe, p0 = (t - e * tpe) * kEncM;
+        for (int c = 0; c < cpt; c++, g++) {
+            const int st = g % kEncStages;
+            int ok = 1;
+            if (lane == 0) ok = mbar_wait(smem_addr(bars + st), (g / kEncStages) & 1, nullptr) ? 1 : 0;
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (ok) {
+                mbar_wait(smem_addr(bars + st), (g / kEncStages) & 1, nullptr);
+                const float* box = reinterpret_cast<const float*>(ring + st * kStageBytes);
+                const int rows = c == P.nfull ? P.tail_rows : 64;
+                const int px = tid & (kEncM - 1), part = tid >> 7;
+                for (int o = part; o < rows / 8; o += kEncParts) {
+                    float f[8];
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        const int k = 64 * c + 8 * o + j;
+                        f[j] = k < P.ci ? box[(8 * o + j) * kEncM + px] : 0.0f;
+                    }
+                    __half2 h0 = __floats2half2_rn(f[0], f[1]), h1 = __floats2half2_rn(f[2], f[3]);
+                    __half2 h2 = __floats2half2_rn(f[4], f[5]), h3 = __floats2half2_rn(f[6], f[7]);
+                    uint4 pk;
+                    pk.x = *reinterpret_cast<uint32_t*>(&h0);
+                    pk.y = *reinterpret_cast<uint32_t*>(&h1);
+                    pk.z = *reinterpret_cast<uint32_t*>(&h2);
+                    pk.w = *reinterpret_cast<uint32_t*>(&h3);
+                    *reinterpret_cast<uint4*>(sA + sw128_offset(px, 64 * c + 8 * o)) = pk;
+                }
+                fence_proxy_async();  // generic-proxy stores -> tensor-core reads
+            } else if (lane == 0) {
+                atomicExch(P.err, 21);
+            }
+            // the box is consumed (or abandoned) by every thread: refill its slot
+            alive = __syncthreads_and(ok) != 0;
+            if (!alive) break;
+            if (tid == 0 && g + kEncStages < nchunks) issue(g + kEncStages);
+        }
+        if (!alive) break;
+        if (tid == 0) {
+            tc_fence_after();
+            for (int kk = 0; kk < ksteps; kk++) {
+                const int at = kk >> 2, wi = kk & 3;
+                mma_f16(tmem, sdesc_sw128(aA + at * kAtomBytes + wi * 32),
+                        sdesc_sw128(aB + at * kAtomBytes + wi * 32), idesc, kk > 0 ? 1u : 0u);
+            }
+            mma_commit(mma_bar);
+        }
+        mma_out = true;
+        int ok = 1;
+        if (lane == 0) ok = mbar_wait(mma_bar, mphase, nullptr) ? 1 : 0;
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (ok) {
+            mbar_wait(mma_bar, mphase, nullptr);
+            mma_out = false;
+            tc_fence_after();
+            // warp w: TMEM lane quarter w % 4 (pixels 32 (w % 4) ..), output
+            // channels 32 (w / 4) ..; staged as [co][128 pixels] fp16
+            const int q = warp & 3, cb = 32 * (warp >> 2);
+            float acc[32];
+            tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + cb, acc);
+            __half* stg = reinterpret_cast<__half*>(sA);
+#pragma unroll
+            for (int j = 0; j < 32; j++) {
+                const int co = cb + j;
+                stg[co * kEncM + 32 * q + lane] = __float2half_rn(fmaxf(acc[j] + sbias[co], 0.0f));
+            }
+        } else if (lane == 0) {
+            atomicExch(P.err, 20);
+        }
+        tc_fence_before();
+        alive = __syncthreads_and(ok) != 0;
+        if (alive) {
+            const uint4* stg = reinterpret_cast<const uint4*>(sA);
+            __half* oe = P.out + (size_t)e * kEncCo * hw + p0;
+#pragma unroll
+            for (int j = 0; j < kEncCo * kEncM / 8 / kEncThreads; j++) {
+                const int cc = tid + kEncThreads * j;  // co = cc / 16, 8 pixels each
+                const int co = cc >> 4, x8 = (cc & 15) * 8;
+                if (p0 + x8 < hw) __stcs(reinterpret_cast<uint4*>(oe + (size_t)co * hw + x8), stg[cc]);
+            }
+        }
+        __syncthreads();  // the staged outputs are read before the next tile's operand
+    }
+    if (!alive && tid == 0) {
+        // boxes still in flight and an abandoned MMA group: let them land (bounded)
+        for (int gi = g; gi < issued; gi++)
+            mbar_wait(smem_addr(bars + gi % kEncStages), (gi / kEncStages) & 1, nullptr);
+        if (mma_out) mbar_wait(mma_bar, mphase, nullptr);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 128);
+    }
+}
+
 }  // namespace
 
 int dc_set_corr_encoder_impl(dc_ctx* ctx, const float* weight, const float* bias, int co,
@@ -223,9 +407,35 @@ int dc_launch_encoder(dc_ctx* ctx, const float* corr, int M, void* out, cudaStre
     P.M = M;
     P.ci = ctx->cfg.levels * (2 * ctx->cfg.radius + 1) * (2 * ctx->cfg.radius + 1);
     P.hw = ctx->hw;
-    const size_t smem = 2 * kOperandBytes + 64 + 1024;
     const int ntiles = (ctx->hw + kEncM - 1) / kEncM * M;
     const int grid = ntiles < ctx->num_sms ? ntiles : ctx->num_sms;
+    if (ctx->hw % 8 == 0 && ((uintptr_t)corr & 15) == 0 && ((uintptr_t)out & 15) == 0) {
+        EncTmaParams T;
+        T.wimg = P.wimg;
+        T.bias = P.bias;
+        T.out = P.out;
+        T.err = P.err;
+        T.M = M;
+        T.ci = P.ci;
+        T.hw = P.hw;
+        T.nfull = P.ci / 64;
+        T.tail_rows = (P.ci - 64 * T.nfull + 15) / 16 * 16;
+        alignas(64) unsigned char mf[128], mt[128];
+        const unsigned long long rows = (unsigned long long)M * P.ci;
+        if (dc_tmap_2d_f32(mf, corr, (unsigned long long)P.hw, rows, kEncM, 64) != DC_OK ||
+            (T.tail_rows > 0 &&
+             dc_tmap_2d_f32(mt, corr, (unsigned long long)P.hw, rows, kEncM, T.tail_rows) != DC_OK))
+            return dc_fail(ctx, DC_ERR_CUDA, "cuTensorMapEncodeTiled (corr features) failed");
+        if (T.tail_rows == 0) memcpy(mt, mf, sizeof(mt));
+        const size_t tsmem = 2 * kOperandBytes + kEncStages * kStageBytes + 64 +
+                             kEncCo * sizeof(float) + 1024;
+        cudaFuncSetAttribute(corr_encoder_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)tsmem);
+        corr_encoder_tma_kernel<<<grid, kEncThreads, tsmem, s>>>(
+            *reinterpret_cast<const CUtensorMap*>(mf), *reinterpret_cast<const CUtensorMap*>(mt), T);
+        return dc_check_launch(ctx, "corr_encoder_tma_kernel");
+    }
+    const size_t smem = 2 * kOperandBytes + 64 + 1024;
     cudaFuncSetAttribute(corr_encoder_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem);
     corr_encoder_kernel<<<grid, kEncThreads, smem, s>>>(P);

@@ -157,6 +157,11 @@ int dc_launch_pool2x2(const float* in, float* out, long long N, int H, int W,
                       cudaStream_t s);
 int dc_launch_lookup(dc_ctx* ctx, const float* const* vols, const float* coords, float* out,
                      int M, bool single_edge_arith, cudaStream_t s);
+// A 2-D tensor map (CUtensorMap storage, 128 bytes) over a row-major fp32
+// matrix [rows][cols] with boxes of box_rows x box_cols, no swizzle, elements
+// outside the matrix read as zeros.  cols * 4 must be a multiple of 16.
+int dc_tmap_2d_f32(void* tmap, const void* base, unsigned long long cols,
+                   unsigned long long rows, unsigned box_cols, unsigned box_rows);
 bool dc_tc_supported(const dc_ctx* ctx);
 int dc_tc_prepare(dc_ctx* ctx);
 int dc_launch_tc(dc_ctx* ctx, const int* ii, const int* jj, int M, const float* coords,

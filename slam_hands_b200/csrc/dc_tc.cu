@@ -1062,6 +1062,21 @@ extern "C" int dc_tc_trace_read(long long* host) {
 }
 #endif
 
+int dc_tmap_2d_f32(void* tmap, const void* base, unsigned long long cols,
+                   unsigned long long rows, unsigned box_cols, unsigned box_rows) {
+    EncodeTiledFn enc = get_encode();
+    if (!enc) return DC_ERR_CUDA;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)cols * 4};
+    cuuint32_t box[2] = {box_cols, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(reinterpret_cast<CUtensorMap*>(tmap), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                           const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? DC_OK : DC_ERR_CUDA;
+}
+
 bool dc_tc_supported(const dc_ctx* ctx) {
     const int p = ctx->cfg.precision;
     return (p == DC_PREC_FP16 || p == DC_PREC_BF16 || p == DC_PREC_TF32 || p == DC_PREC_FP32X3) &&
