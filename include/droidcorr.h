@@ -121,7 +121,9 @@ int dc_destroy(dc_ctx* ctx);
 const char* dc_last_error(const dc_ctx* ctx);
 const char* dc_status_string(int status);
 
-/* Bytes of device memory the context holds. */
+/* Bytes of device memory the context holds: the packed store and its sync
+ * page, the error word and lists, and what later calls allocated (encoder
+ * weights, tile-order scratch). */
 long long dc_context_bytes(const dc_ctx* ctx);
 
 /* Pack `count` feature maps into store slots first_slot .. first_slot+count-1

@@ -142,6 +142,7 @@ int dc_create(const dc_config* cfg, dc_ctx** out) {
     // one small allocation: the device error word, then the scatter-mean lists
     // (dc_scatter_mean: edge order, list offsets and mean scales, max_edges each)
     const size_t small_words = 32 + 3 * (size_t)c.max_edges + 1;
+    ctx->other_bytes += (long long)(small_words * sizeof(int));
     if (cudaMalloc(&ctx->dev_err, small_words * sizeof(int)) != cudaSuccess ||
         cudaMemset(ctx->dev_err, 0, sizeof(int)) != cudaSuccess) {
         cudaFree(ctx->store);
@@ -179,7 +180,9 @@ int dc_destroy(dc_ctx* ctx) {
 
 const char* dc_last_error(const dc_ctx* ctx) { return ctx ? ctx->err.c_str() : "null context"; }
 
-long long dc_context_bytes(const dc_ctx* ctx) { return ctx ? ctx->store_bytes : 0; }
+long long dc_context_bytes(const dc_ctx* ctx) {
+    return ctx ? ctx->store_bytes + kSyncPageBytes + ctx->other_bytes : 0;
+}
 
 long long dc_launch_count(const dc_ctx* ctx) { return ctx ? ctx->launches : 0; }
 
@@ -207,6 +210,7 @@ int dc_set_tile_order(dc_ctx* ctx, int order) {
             cudaGetLastError();
             return dc_fail(ctx, DC_ERR_NO_MEMORY, "tile permutation scratch");
         }
+        ctx->other_bytes += (long long)(words * sizeof(int));
     }
     ctx->tile_order = order;
     return DC_OK;

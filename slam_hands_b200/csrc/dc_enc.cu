@@ -382,6 +382,7 @@ int dc_set_corr_encoder_impl(dc_ctx* ctx, const float* weight, const float* bias
             ctx->enc_w = nullptr;
             return dc_fail(ctx, DC_ERR_NO_MEMORY, "encoder weights");
         }
+        ctx->other_bytes += (long long)(kWeightBytes + kEncCo * sizeof(float));
     }
     float* b = reinterpret_cast<float*>(static_cast<char*>(ctx->enc_w) + kWeightBytes);
     enc_pack_weights_kernel<<<(kEncCo * kEncK + 255) / 256, 256, 0, s>>>(

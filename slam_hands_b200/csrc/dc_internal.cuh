@@ -34,6 +34,7 @@ struct dc_ctx {
     void* store = nullptr;  // device
     void* src_store = nullptr;  // another process's store, opened by dc_store_attach_source
     long long store_bytes = 0;
+    long long other_bytes = 0;  // every other device allocation of the context (scratch, weights)
     int num_sms = 148;
     int max_ctas = 0;  // cap on the CTAs of the persistent fused kernel (0: one per SM)
     long long launches = 0;
