@@ -80,6 +80,7 @@ static_assert(kChunkN <= kAccCols && kChunkN % 16 == 0, "MMA N");
 static_assert(kChunkStrips <= 32, "one bit per strip of a chunk");
 static_assert(kWarpBlocks >= 1, "every epilogue warp drains at least one 64-column block");
 static_assert(kSubWarps == 2 || kSubWarps == 4, "epilogue warps per lane quarter");
+static_assert(kTileM == 4 * 32, "one 4-row source gather per producer lane");
 
 // Per-level constants of the target boxes (host-computed): a box holds br rows
 // of wbox pixels (wbox a multiple of 8, br * wbox <= 256); a row wider than
@@ -517,49 +518,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) mbar_arrive(bar(kBarSFull + tb));  // release: schedule
             const TileInfo ti = tinfo[tb];
             const LevelSched* sch = sched_base + tb * DC_MAX_LEVELS;
-            if (lane == 0 && ti.n > 0) {
+            if (ti.n > 0) {
                 // The first kStagesB target-row chunks do not depend on the single
                 // source-tile buffer: issue them first, so their loads overlap the
                 // previous tile's last MMAs; then wait until those MMAs release the
-                // source buffer and load this tile's source pixels.
+                // source buffer and load this tile's source pixels; then the rest.
                 const int pre = min(kStagesB, ti.n);
-                int lv = 0;
-                for (int c = 0; c <= ti.n; c++) {
-                    if (c == pre) {
-                        if (na >= 1 && !mbar_wait(bar(kBarAEmpty), (na - 1) & 1, abort, P.wait_ns)) {
-                            raise_abort(abort, P.err, 3);
-                            break;
-                        }
-                        if (!(P.stall && na == 0)) {
-                            mbar_arrive_expect_tx(bar(kBarAFull), P.atoms * kTileM * kRowBytes);
-                            const int rbase =
-                                (int)((long long)ti.si * g.frame_rows + P.a_off + g.row0[0]);
-                            if (ti.gather) {
-                                // permuted tile: 4 source rows per gather (512 bytes)
-                                for (int k = 0; k < P.atoms; k++)
-#pragma unroll 1
-                                    for (int j = 0; j < kTileM / 4; j++)
-                                        tma_gather4(sA + k * kTileM * kRowBytes + j * 4 * kRowBytes,
-                                                    &maps.a_rows, k * 64, rbase + arows[4 * j],
-                                                    rbase + arows[4 * j + 1], rbase + arows[4 * j + 2],
-                                                    rbase + arows[4 * j + 3], bar(kBarAFull));
-                            } else {
-                                for (int k = 0; k < P.atoms; k++)
-                                    tma_load_2d(sA + k * kTileM * kRowBytes, &maps.a, k * 64,
-                                                rbase + ti.p0, bar(kBarAFull));
-                            }
-                            a_issued = 1;
-                            a_parity = na & 1;
-                        }
-                    }
-                    if (c == ti.n) break;
+                int lv = 0, ok = 1;
+                // (lane 0) target-row chunk c of this tile into the next stage
+                auto issue_chunk = [&](int c) -> int {
                     while (c >= sch[lv].first + sch[lv].count) lv++;
                     const int s = gc % kStagesB;
                     const long long t0 = DC_PROF_NOW();
                     if (gc >= kStagesB &&
                         !mbar_wait(bar(kBarEmpty + s), ((gc / kStagesB) - 1) & 1, abort, P.wait_ns)) {
                         raise_abort(abort, P.err, 4);
-                        break;
+                        return 0;
                     }
                     w_a += DC_PROF_NOW() - t0;
                     DC_TRACE(0, gc);
@@ -571,7 +545,43 @@ __global__ void __launch_bounds__(kThreads, 1)
                                     k * 64, cg.x0, cg.y0, ti.sj, bar(kBarFull + s));
                     gc++;
                     last_gc = gc;
+                    return 1;
+                };
+                if (lane == 0)
+                    for (int c = 0; c < pre && ok; c++) ok = issue_chunk(c);
+                int aload = 0;
+                if (lane == 0 && ok) {
+                    if (na >= 1 && !mbar_wait(bar(kBarAEmpty), (na - 1) & 1, abort, P.wait_ns)) {
+                        raise_abort(abort, P.err, 3);
+                        ok = 0;
+                    } else if (!(P.stall && na == 0)) {
+                        mbar_arrive_expect_tx(bar(kBarAFull), P.atoms * kTileM * kRowBytes);
+                        a_issued = 1;
+                        a_parity = na & 1;
+                        aload = 1;
+                    }
                 }
+                // (the shuffles also order lane 0's expect-tx before the gathers)
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                aload = __shfl_sync(0xffffffffu, aload, 0);
+                if (aload) {
+                    const int rbase = (int)((long long)ti.si * g.frame_rows + P.a_off + g.row0[0]);
+                    if (ti.gather) {
+                        // permuted tile: lane L gathers source rows 4L .. 4L + 3 (512
+                        // bytes per K atom), all lanes at once
+                        const int r0 = rbase + arows[4 * lane], r1 = rbase + arows[4 * lane + 1];
+                        const int r2 = rbase + arows[4 * lane + 2], r3 = rbase + arows[4 * lane + 3];
+                        for (int k = 0; k < P.atoms; k++)
+                            tma_gather4(sA + k * kTileM * kRowBytes + lane * 4 * kRowBytes,
+                                        &maps.a_rows, k * 64, r0, r1, r2, r3, bar(kBarAFull));
+                    } else if (lane == 0) {
+                        for (int k = 0; k < P.atoms; k++)
+                            tma_load_2d(sA + k * kTileM * kRowBytes, &maps.a, k * 64,
+                                        rbase + ti.p0, bar(kBarAFull));
+                    }
+                }
+                if (lane == 0 && ok)
+                    for (int c = pre; c < ti.n && ok; c++) ok = issue_chunk(c);
             }
             if (ti.n > 0) na++;
             __syncwarp();

@@ -103,13 +103,13 @@ def test_window_row_order_c5_oracle(cuda, oracle):
 def test_tile_order_scratch_is_counted_once(cuda):
     h, w, M = 24, 32, 5
     dc = DroidCorrelation(h, w, precision="fp16", alpha=0.0625, max_frames=2, max_edges=M)
-    before = dc.context_bytes()
+    before = dc.context_bytes
     dc.set_tile_order("auto")
-    grown = dc.context_bytes()
+    grown = dc.context_bytes
     assert grown - before == M * (3 * h * w + 1) * 4
     dc.set_tile_order("window_row")
     dc.set_tile_order("source")
-    assert dc.context_bytes() == grown  # the scratch is allocated once and kept
+    assert dc.context_bytes == grown  # the scratch is allocated once and kept
     with pytest.raises(Exception):
         dc.set_tile_order("rows")
     dc.close()
