@@ -371,7 +371,7 @@ int dc_set_max_ctas(dc_ctx* ctx, int max_ctas);
  *                        scattered output stores and a gathered source tile;
  *   DC_ORDER_AUTO        the pre-pass picks, per edge, the window-row order
  *                        when the level-0 target pixels it saves per tile
- *                        reach 16 x the output channels (3136 at r = 3, four
+ *                        reach 8 x the output channels (1568 at r = 3, four
  *                        levels), else the source order.
  * Results do not depend on the order (each output is computed from its own
  * pixel's dot products).  The first call with an order other than

@@ -851,10 +851,11 @@ constexpr int kBinMaxKeys = 512;
 // x the output channels: the gain grows with the target pixels no longer
 // multiplied, the cost (reordering the tile's outputs, one read and one write
 // of 128 x channels floats) with the channels.  Measured on one B200 (fp16,
-// 196 channels, so a threshold of 3136): ~530 pixels saved per tile (48x64,
-// flow noise N(0, 2 px)): 1.5x slower; ~2200 (48x64, N(0, 8 px)): 3 % slower;
-// ~3500 (54x96, N(0, 8 px)): 1.4x faster.
-constexpr int kAutoPxPerChannel = 16;
+// 196 channels, so a threshold of 1568), window-row against source order:
+// ~530 pixels saved per tile (48x64, flow noise N(0, 2 px)): 1.4x slower;
+// ~1350 (54x96, N(0, 3 px)): 1.03x faster; ~2200 (48x64, N(0, 8 px)): 1.12x
+// faster; ~3500 (54x96, N(0, 8 px)): 1.6x faster.
+constexpr int kAutoPxPerChannel = 8;
 
 __device__ __forceinline__ int bin_key(float y, int H0) {
     // fmaxf / fminf return the other operand for a NaN: NaN sorts first
