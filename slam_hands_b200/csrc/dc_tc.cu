@@ -28,6 +28,13 @@
 //      reading window column x at slot column (bx mod 8) + x, and stores them as
 //      out[e][l*(2r+1)^2 + a*(2r+1) + b][p] (consecutive pixels per warp).
 //
+// A tile is 128 consecutive source pixels, or, in the window-row tile order
+// (dc_set_tile_order), 128 positions of a per-edge permutation that groups
+// pixels by the row of their level-0 window: tile_order_kernel sorts each
+// edge first, the producer then gathers the source rows with tile::gather4,
+// the epilogue writes outputs at the tile position, and unpermute_rows_kernel
+// moves them to pixel order after the call.
+//
 // Warp roles (320 threads): warp 0 schedules tiles and issues TMA, warp 1
 // allocates TMEM and issues MMAs (one elected lane each), warps 2..9 are the
 // epilogue.  Warp w reads TMEM lanes 32*(w%4) .. 32*(w%4)+31, i.e. tile pixels
@@ -447,7 +454,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int k = 0; k < kTileM / 32; k++) {
                 cx[k] = cxn[k];
                 cy[k] = cyn[k];
-                // the source rows to gather (read by lane 0 in the issue loop below)
+                // the source rows to gather (lane L reads rows 4L .. 4L + 3 below)
                 if (ga) arows[lane + 32 * k] = (unsigned short)pxn[k];  // hw <= DC_MAX_HW < 2^16
             }
             const int si = sin_, sj = sjn;
