@@ -79,6 +79,9 @@ def test_null_context_is_an_error_not_a_crash():
     assert lib.dc_destroy(None) == L.DC_OK
     assert lib.dc_pool_2x2(None, None, 0, 4, 4, None) == L.DC_OK  # empty: nothing to do
     assert lib.dc_pool_2x2(None, None, 1, 4, 4, None) == L.DC_ERR_INVALID_ARG
+    for order in (L.DC_ORDER_SOURCE, L.DC_ORDER_WINDOW_ROW, L.DC_ORDER_AUTO, 7):
+        assert lib.dc_set_tile_order(None, order) == L.DC_ERR_INVALID_ARG
+    assert lib.dc_context_bytes(None) == 0
 
 
 def test_product_path_does_not_reference_the_oracle():
