@@ -18,8 +18,9 @@
 // accumulator; each warp reads 32 outputs of its lane quarter's 32 pixels back
 // (tcgen05.ld), adds the bias, applies the ReLU, rounds to fp16 and stores
 // 64-byte rows.
-// That kernel serves grids whose h*w is not a multiple of 8; for the others
-// corr_encoder_tma_kernel streams the features with TMA (below).
+// That kernel serves grids whose h*w is not a multiple of 8 or is below 128;
+// for the others corr_encoder_tma_kernel streams the features with TMA
+// (below).
 // The waits for the MMAs and the boxes are bounded (2 s) and report through
 // the context's device error word.
 #include <cuda.h>
@@ -410,7 +411,10 @@ int dc_launch_encoder(dc_ctx* ctx, const float* corr, int M, void* out, cudaStre
     P.hw = ctx->hw;
     const int ntiles = (ctx->hw + kEncM - 1) / kEncM * M;
     const int grid = ntiles < ctx->num_sms ? ntiles : ctx->num_sms;
-    if (ctx->hw % 8 == 0 && ((uintptr_t)corr & 15) == 0 && ((uintptr_t)out & 15) == 0) {
+    // TMA path: rows of whole 16-byte runs, aligned buffers, and at least one
+    // full 128-pixel box per row
+    if (ctx->hw % 8 == 0 && ctx->hw >= kEncM && ((uintptr_t)corr & 15) == 0 &&
+        ((uintptr_t)out & 15) == 0) {
         EncTmaParams T;
         T.wimg = P.wimg;
         T.bias = P.bias;
